@@ -1,0 +1,184 @@
+/*
+ * shield_b200 — C ABI of the B200-native Shieldstral scoring prefill.
+ *
+ * This is the drop-in boundary for the hot path of curiosity-ai/llm-shield:
+ * everything under MinistralModel.ForwardSelectedAsync (token ids -> yes/no
+ * logits) and QuantMatMul.ForwardAsync/ForwardRowsAsync (the quantized GEMM)
+ * runs on sm_100a behind these entry points.  The .NET surface
+ * (ShieldstralModerator, ModerationResult, GgufFile, TekkenTokenizer,
+ * ModelConfig) stays where it is and calls in through P/Invoke.
+ *
+ * Conventions (mirroring the reference):
+ *  - Weights are uploaded once, byte-for-byte in their GGUF block layout
+ *    (GgufFile.GetTensorPointer, Gguf/GgufFile.cs:195-199); the caller keeps
+ *    ownership of the bytes it passes.
+ *  - Errors are status codes; shield_last_error() gives the message of the
+ *    calling thread's last failure.  Codes map to the reference's exceptions:
+ *    ARG -> ArgumentException, RANGE -> ArgumentOutOfRangeException,
+ *    UNSUPPORTED -> NotSupportedException, CANCELLED -> OperationCanceledException,
+ *    SHAPE -> InvalidDataException (MinistralModel.cs:110-123).
+ *  - A context is not re-entrant: one call at a time, as one MinistralModel
+ *    instance is not thread-safe (MinistralModel.cs:21-22).  Internally a
+ *    context drives one host thread and one CUDA stream per selected GPU.
+ *  - Results do not depend on how requests are batched or on how many GPUs
+ *    the context spans (the reference's MatMulTilingTests.cs:42-95 invariants).
+ *
+ * Citations are path:line within the reference project.
+ */
+#ifndef SHIELD_B200_H
+#define SHIELD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct shield_ctx shield_ctx;
+typedef int32_t shield_status;
+
+enum {
+    SHIELD_OK = 0,
+    SHIELD_ERR_ARG = 1,          /* ArgumentException */
+    SHIELD_ERR_RANGE = 2,        /* ArgumentOutOfRangeException */
+    SHIELD_ERR_UNSUPPORTED = 3,  /* NotSupportedException */
+    SHIELD_ERR_CANCELLED = 4,    /* OperationCanceledException */
+    SHIELD_ERR_CUDA = 5,         /* a CUDA runtime or launch failure */
+    SHIELD_ERR_TIMEOUT = 6,      /* a device-side wait gave up (bounded spin) */
+    SHIELD_ERR_SHAPE = 7,        /* InvalidDataException: tensors disagree with the config */
+    SHIELD_ERR_STATE = 8,        /* called before configuration / upload */
+    SHIELD_ERR_NOMEM = 9         /* device or pinned host memory exhausted */
+};
+
+/* GGML type ids (Gguf/GgmlType.cs:10-44); the legacy 32-blocks are the ones
+ * with an integer kernel (IntegerGemm.Supports, Quantization/IntegerGemm.cs:58-65). */
+enum {
+    SHIELD_TYPE_F32 = 0,
+    SHIELD_TYPE_F16 = 1,
+    SHIELD_TYPE_Q4_0 = 2,
+    SHIELD_TYPE_Q4_1 = 3,
+    SHIELD_TYPE_Q5_0 = 6,
+    SHIELD_TYPE_Q5_1 = 7,
+    SHIELD_TYPE_Q8_0 = 8
+};
+
+/*
+ * Model hyperparameters, the fields of ModelConfig (Model/ModelConfig.cs:12-60)
+ * the forward pass uses.  RoPE frequencies are computed from the YaRN fields
+ * exactly as the Rope constructor does (Model/Rope.cs:33-106) unless the caller
+ * passes its own table (n_rope_freqs > 0: Rope.Frequencies and
+ * Rope.MagnitudeScale as computed by the unchanged C# code).
+ */
+typedef struct shield_config {
+    int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+    float rms_eps;
+    float rope_freq_base;
+    int32_t rope_dim;
+    float rope_scale_factor;
+    int32_t rope_yarn; /* ModelConfig.YarnActive */
+    int32_t rope_orig_ctx;
+    float yarn_beta_fast, yarn_beta_slow, yarn_ext_factor, yarn_mscale, yarn_mscale_all_dim, rope_attn_factor;
+    float attn_temperature_beta; /* ModelConfig.AttentionTemperatureScale */
+    int32_t n_rope_freqs;        /* 0, or rope_dim/2 with rope_freqs set */
+    const float *rope_freqs;
+    float rope_mscale;
+    int32_t max_positions;    /* longest request accepted; 0 = 8192 */
+    int32_t max_batch_tokens; /* tokens per device micro-batch; 0 = 16384 */
+} shield_config;
+
+/* Opens one context over the GPUs whose bits are set in device_mask
+ * (bit i = CUDA device i); 0 selects device 0.  Each selected GPU will hold a
+ * full replica of the uploaded weights. */
+shield_status shield_open(int32_t device_mask, shield_ctx **out);
+void shield_close(shield_ctx *ctx);
+/* Number of GPUs the context spans. */
+int32_t shield_device_count(const shield_ctx *ctx);
+
+/* ModelConfig.FromGguf's result (ModelConfig.cs:62-112), set once before upload. */
+shield_status shield_set_config(shield_ctx *ctx, const shield_config *cfg);
+
+/*
+ * Copies one GGUF tensor's bytes, unchanged, to every GPU of the context
+ * (WeightMatrix.From / VectorParameter.From, Numerics/WeightMatrix.cs:53-90).
+ * name: the GGUF name ("token_embd.weight", "blk.3.attn_q.weight", ...);
+ * rows = output features (ne[1]), cols = input features (ne[0]).
+ * Quantized matrices must be Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 with cols % 32 == 0;
+ * norm vectors may be F32 or F16.  nbytes must equal rows * row bytes.
+ */
+shield_status shield_upload_tensor(shield_ctx *ctx, const char *name, uint32_t ggml_type, int64_t rows,
+                                   int64_t cols, const void *bytes, size_t nbytes);
+
+/*
+ * Scores a ragged batch of independent requests: ShieldstralModerator's
+ * ModerateAsync from the prompt's token ids on (ShieldstralModerator.cs:246-263),
+ * i.e. MinistralModel.ForwardSelectedAsync on an empty cache followed by
+ * Score (ShieldstralModerator.cs:348-364).
+ *   ids[offsets[r] .. offsets[r+1])   token ids of request r (n_req + 1 offsets)
+ *   verdict_ids[0 .. n_yes)           "yes" vocabulary rows; then n_no "no" rows
+ *   yes[r], no[r], score[r]           best yes logit, best no logit, 2-way softmax
+ *   logits (optional)                 n_req x (n_yes + n_no) verdict logits
+ *   cancel (optional)                 polled between layers; non-zero cancels
+ * Requests are sharded across the context's GPUs; results do not depend on
+ * the sharding.  The verdict is score > 0.5 (ModerationResult.IsUnsafe).
+ */
+shield_status shield_score_batch(shield_ctx *ctx, const int32_t *ids, const int64_t *offsets, int32_t n_req,
+                                 const int32_t *verdict_ids, int32_t n_yes, int32_t n_no, float *yes, float *no,
+                                 float *score, float *logits, const volatile int32_t *cancel);
+
+/*
+ * QuantMatMul.ForwardAsync / ForwardRowsAsync (Numerics/QuantMatMul.cs:71-110)
+ * on one GPU of the context, host buffers in and out:
+ *   y[t, i] = dot(x[t, :], W[row(i), :]),  x: M x cols, y: M x n_out
+ * with row(i) = row_ids[i] when row_ids is non-null (n_out = n_rows), else i
+ * (n_out = rows).  Activations are quantized once per call
+ * (IntegerGemm.QuantizeActivations) and every output is bit-identical to the
+ * reference's integer GEMM arithmetic.
+ */
+shield_status shield_qmatmul(shield_ctx *ctx, int32_t device, const char *weight, const float *x, int64_t M,
+                             float *y, const int32_t *row_ids, int32_t n_rows);
+
+/* As shield_qmatmul with device-resident x and y (full row range), enqueued on
+ * the context's stream for that GPU without synchronizing. */
+shield_status shield_qmatmul_device(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x,
+                                    int64_t M, float *d_y);
+
+/* The raw per-block int32 dot products i = -z*Σa + Σ u*a of the integer GEMM
+ * (IntegerGemm.cs:384-397): dots[(t*rows + n)*(cols/32) + b], for checking
+ * bit-exactness.  path: 0 = the GEMM path shield_qmatmul would take,
+ * 1 = CUDA-core kernel, 2 = tensor-core kernel. */
+shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const char *weight, const float *x,
+                                      int64_t M, int32_t *dots, int32_t path);
+
+/* Which GEMM kernel the context uses: 0 = automatic (tensor cores where the
+ * shape allows), 1 = CUDA-core kernel only, 2 = tensor cores only (shapes they
+ * do not take fail with SHIELD_ERR_UNSUPPORTED). For cross-checking. */
+shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path);
+
+/* Intermediate tensors of one layer, named as MinistralModel's
+ * IActivationSink names them (MinistralModel.cs:212-237). */
+enum {
+    SHIELD_ACT_OUTPUT = 0,        /* blk.N.output         n x hidden */
+    SHIELD_ACT_Q_ROPE = 1,        /* blk.N.q_rope         n x n_heads*head_dim */
+    SHIELD_ACT_K_ROPE = 2,        /* blk.N.k_rope         n x n_kv_heads*head_dim */
+    SHIELD_ACT_V = 3,             /* blk.N.v              n x n_kv_heads*head_dim */
+    SHIELD_ACT_ATTN_WEIGHTED = 4, /* blk.N.attn_weighted  n x n_heads*head_dim */
+    SHIELD_ACT_POST_ATTN = 5,     /* blk.N.post_attn      n x hidden */
+    SHIELD_ACT_ATTN_NORM = 6      /* blk.N.attn_norm      n x hidden */
+};
+
+/* One request through the model on one GPU with tensor `what` of layer
+ * `layer` copied out to `out`, for layer-by-layer parity checks. */
+shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int32_t *ids, int32_t n,
+                                      int32_t layer, int32_t what, float *out);
+
+/* The CUDA stream (cudaStream_t) the context enqueues work for `device` on. */
+shield_status shield_device_stream(shield_ctx *ctx, int32_t device, void **stream);
+
+/* Message of the calling thread's most recent failure ("" if none). */
+const char *shield_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

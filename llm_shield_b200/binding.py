@@ -1,0 +1,214 @@
+"""ctypes binding of the C ABI in include/shield_b200.h (libshield_b200.so).
+
+This is the harness-side view of the boundary a .NET host would P/Invoke:
+the same entry points, the same arguments, host numpy buffers.  There is no
+fallback: if the CUDA library is missing or no GPU is visible, calls fail.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _build
+from . import synth
+
+ACT_OUTPUT, ACT_Q_ROPE, ACT_K_ROPE, ACT_V, ACT_ATTN_WEIGHTED, ACT_POST_ATTN, ACT_ATTN_NORM = range(7)
+OK, ERR_ARG, ERR_RANGE, ERR_UNSUPPORTED, ERR_CANCELLED, ERR_CUDA, ERR_TIMEOUT, ERR_SHAPE, ERR_STATE, ERR_NOMEM = range(10)
+
+
+class ShieldError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+class ShieldArgumentOutOfRange(ShieldError, IndexError):
+    pass
+
+
+class ShieldCancelled(ShieldError):
+    pass
+
+
+class ShieldConfig(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32),
+        ("head_dim", C.c_int32), ("ffn", C.c_int32), ("vocab", C.c_int32), ("rms_eps", C.c_float),
+        ("rope_freq_base", C.c_float), ("rope_dim", C.c_int32), ("rope_scale_factor", C.c_float),
+        ("rope_yarn", C.c_int32), ("rope_orig_ctx", C.c_int32), ("yarn_beta_fast", C.c_float),
+        ("yarn_beta_slow", C.c_float), ("yarn_ext_factor", C.c_float), ("yarn_mscale", C.c_float),
+        ("yarn_mscale_all_dim", C.c_float), ("rope_attn_factor", C.c_float),
+        ("attn_temperature_beta", C.c_float), ("n_rope_freqs", C.c_int32),
+        ("rope_freqs", C.POINTER(C.c_float)), ("rope_mscale", C.c_float),
+        ("max_positions", C.c_int32), ("max_batch_tokens", C.c_int32),
+    ]
+
+
+EXPORTS = [
+    "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
+    "shield_score_batch", "shield_qmatmul", "shield_qmatmul_device", "shield_debug_block_dots",
+    "shield_set_gemm_path", "shield_debug_activation", "shield_device_stream", "shield_last_error",
+]
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libshield_b200.so (building it in-tree if it is absent)."""
+    global _lib
+    if _lib is None:
+        path = _build.main_lib_path()
+        if not path.exists():
+            _build.build_main()
+        L = C.CDLL(str(path))
+        P = C.c_void_p
+        L.shield_open.argtypes = [C.c_int32, C.POINTER(P)]
+        L.shield_close.argtypes = [P]
+        L.shield_close.restype = None
+        L.shield_device_count.argtypes = [P]
+        L.shield_set_config.argtypes = [P, C.POINTER(ShieldConfig)]
+        L.shield_upload_tensor.argtypes = [P, C.c_char_p, C.c_uint32, C.c_int64, C.c_int64, P, C.c_size_t]
+        L.shield_score_batch.argtypes = [P, P, P, C.c_int32, P, C.c_int32, C.c_int32, P, P, P, P, P]
+        L.shield_qmatmul.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, P, C.c_int32]
+        L.shield_qmatmul_device.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
+        L.shield_debug_block_dots.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, C.c_int32]
+        L.shield_set_gemm_path.argtypes = [P, C.c_int32]
+        L.shield_debug_activation.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_int32, P]
+        L.shield_device_stream.argtypes = [P, C.c_int32, C.POINTER(P)]
+        L.shield_last_error.restype = C.c_char_p
+        for name in EXPORTS:
+            f = getattr(L, name)
+            if name not in ("shield_close", "shield_last_error", "shield_device_count"):
+                f.restype = C.c_int32
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc == OK:
+        return
+    msg = (lib().shield_last_error() or b"").decode(errors="replace")
+    if rc == ERR_RANGE:
+        raise ShieldArgumentOutOfRange(rc, msg)
+    if rc == ERR_CANCELLED:
+        raise ShieldCancelled(rc, msg)
+    raise ShieldError(rc, msg)
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def config_from_spec(spec: "synth.ModelSpec", max_positions: int = 0, max_batch_tokens: int = 0) -> ShieldConfig:
+    c = ShieldConfig()
+    c.n_layers, c.hidden, c.n_heads, c.n_kv_heads = spec.n_layers, spec.hidden, spec.n_heads, spec.n_kv_heads
+    c.head_dim, c.ffn, c.vocab, c.rms_eps = spec.head_dim, spec.ffn, spec.vocab, spec.rms_eps
+    c.rope_freq_base, c.rope_dim = spec.rope_theta, spec.head_dim
+    yarn = spec.yarn_factor > 1.0 and spec.yarn_orig_ctx > 0
+    c.rope_scale_factor = spec.yarn_factor if yarn else 1.0
+    c.rope_yarn = int(yarn)
+    c.rope_orig_ctx = spec.yarn_orig_ctx
+    c.yarn_beta_fast, c.yarn_beta_slow, c.yarn_ext_factor = spec.yarn_beta_fast, spec.yarn_beta_slow, 1.0
+    c.yarn_mscale, c.yarn_mscale_all_dim, c.rope_attn_factor = 1.0, 1.0, 1.0
+    c.attn_temperature_beta = spec.attn_temperature_beta
+    c.n_rope_freqs = 0
+    c.rope_mscale = 1.0
+    c.max_positions, c.max_batch_tokens = max_positions, max_batch_tokens
+    return c
+
+
+class ShieldContext:
+    """One shield_ctx spanning the GPUs in device_mask."""
+
+    def __init__(self, device_mask: int = 1):
+        self._h = C.c_void_p()
+        _check(lib().shield_open(device_mask, C.byref(self._h)))
+
+    def close(self):
+        if self._h:
+            lib().shield_close(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def device_count(self) -> int:
+        return lib().shield_device_count(self._h)
+
+    def set_config(self, spec, max_positions: int = 0, max_batch_tokens: int = 0):
+        self.spec = spec
+        c = config_from_spec(spec, max_positions, max_batch_tokens)
+        _check(lib().shield_set_config(self._h, C.byref(c)))
+
+    def upload(self, name: str, qtype: int, rows: int, cols: int, data: np.ndarray):
+        data = np.ascontiguousarray(data, np.uint8)
+        _check(lib().shield_upload_tensor(self._h, name.encode(), qtype, rows, cols, _p(data), data.nbytes))
+
+    def upload_model(self, tensors: dict):
+        for name, t in tensors.items():
+            self.upload(name, t["type"], t["rows"], t["cols"], t["data"])
+
+    def score_batch(self, requests, verdict_ids, n_yes: int, cancel: np.ndarray | None = None):
+        """requests: list of int32 arrays. Returns (yes, no, score, logits)."""
+        lens = np.array([len(r) for r in requests], np.int64)
+        offsets = np.zeros(len(requests) + 1, np.int64)
+        np.cumsum(lens, out=offsets[1:])
+        ids = np.ascontiguousarray(np.concatenate(requests) if requests else np.zeros(0, np.int32), np.int32)
+        return self.score_packed(ids, offsets, verdict_ids, n_yes, cancel)
+
+    def score_packed(self, ids: np.ndarray, offsets: np.ndarray, verdict_ids, n_yes: int, cancel=None):
+        v = np.ascontiguousarray(verdict_ids, np.int32)
+        n_req = offsets.size - 1
+        yes = np.zeros(n_req, np.float32)
+        no = np.zeros(n_req, np.float32)
+        score = np.zeros(n_req, np.float32)
+        logits = np.zeros((n_req, v.size), np.float32)
+        _check(lib().shield_score_batch(self._h, _p(ids), _p(np.ascontiguousarray(offsets, np.int64)), n_req,
+                                        _p(v), n_yes, v.size - n_yes, _p(yes), _p(no), _p(score), _p(logits),
+                                        _p(cancel) if cancel is not None else None))
+        return yes, no, score, logits
+
+    def qmatmul(self, weight: str, x: np.ndarray, M: int, n_out: int, row_ids=None, device: int = 0):
+        x = np.ascontiguousarray(x, np.float32)
+        if row_ids is not None:
+            ids = np.ascontiguousarray(row_ids, np.int32)
+            y = np.zeros((M, ids.size), np.float32)
+            _check(lib().shield_qmatmul(self._h, device, weight.encode(), _p(x), M, _p(y), _p(ids), ids.size))
+        else:
+            y = np.zeros((M, n_out), np.float32)
+            _check(lib().shield_qmatmul(self._h, device, weight.encode(), _p(x), M, _p(y), None, 0))
+        return y
+
+    def qmatmul_device(self, weight: str, d_x: int, M: int, d_y: int, device: int = 0):
+        _check(lib().shield_qmatmul_device(self._h, device, weight.encode(), C.c_void_p(d_x), M, C.c_void_p(d_y)))
+
+    def block_dots(self, weight: str, x: np.ndarray, M: int, rows: int, cols: int, path: int = 0, device: int = 0):
+        x = np.ascontiguousarray(x, np.float32)
+        d = np.zeros((M, rows, cols // 32), np.int32)
+        _check(lib().shield_debug_block_dots(self._h, device, weight.encode(), _p(x), M, _p(d), path))
+        return d
+
+    def set_gemm_path(self, path: int):
+        _check(lib().shield_set_gemm_path(self._h, path))
+
+    def activation(self, ids, layer: int, what: int = ACT_OUTPUT, device: int = 0):
+        """Tensor `what` (ACT_*) of layer `layer` for one request."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        s = self.spec
+        width = {ACT_Q_ROPE: s.qdim, ACT_ATTN_WEIGHTED: s.qdim, ACT_K_ROPE: s.kvdim, ACT_V: s.kvdim}.get(what, s.hidden)
+        out = np.zeros((ids.size, width), np.float32)
+        _check(lib().shield_debug_activation(self._h, device, _p(ids), ids.size, layer, what, _p(out)))
+        return out
+
+    def stream(self, device: int = 0) -> int:
+        s = C.c_void_p()
+        _check(lib().shield_device_stream(self._h, device, C.byref(s)))
+        return s.value or 0

@@ -1,0 +1,882 @@
+// Host runtime of the Shieldstral scoring prefill and its C ABI
+// (include/shield_b200.h): per-GPU weight store, micro-batched forward over a
+// ragged batch of requests, request sharding across GPUs.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <numeric>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "ops.h"
+#include "shield_b200.h"
+
+namespace shield {
+
+struct Error : std::runtime_error {
+    shield_status code;
+    Error(shield_status c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+static thread_local std::string g_last_error;
+
+#define SHIELD_CUDA(x)                                                                                 \
+    do {                                                                                               \
+        cudaError_t e_ = (x);                                                                          \
+        if (e_ != cudaSuccess)                                                                         \
+            throw Error(e_ == cudaErrorMemoryAllocation ? SHIELD_ERR_NOMEM : SHIELD_ERR_CUDA,          \
+                        std::string(#x) + " failed: " + cudaGetErrorString(e_));                     \
+    } while (0)
+
+static int64_t row_bytes_of(int type, int64_t cols) {
+    switch (type) {
+    case T_F32: return cols * 4;
+    case T_F16: return cols * 2;
+    default: {
+        int bb = block_bytes_host(type);
+        return bb && cols % 32 == 0 ? cols / 32 * bb : -1;
+    }
+    }
+}
+
+// ------------------------------------------------------------------ config
+
+struct Config {
+    int n_layers = 0, hidden = 0, n_heads = 0, n_kv_heads = 0, head_dim = 0, ffn = 0, vocab = 0;
+    float eps = 1e-5f;
+    int rope_half = 0;
+    std::vector<float> freqs;
+    float mscale = 1.0f;
+    float temp_beta = 0.0f;
+    int orig_ctx = 0;
+    int max_positions = 8192;
+    int max_batch_tokens = 16384;
+    int qdim() const { return n_heads * head_dim; }
+    int kvdim() const { return n_kv_heads * head_dim; }
+    int max_k() const { return std::max(std::max(hidden, qdim()), ffn); }
+};
+
+static float mscale_term(float scale, float m) { return scale <= 1.0f ? 1.0f : 0.1f * m * logf(scale) + 1.0f; }
+
+// The Rope constructor (Rope.cs:33-106), in float32 as the reference computes it.
+static void rope_freqs(const shield_config &c, std::vector<float> &freqs, float &mscale) {
+    int dim = c.rope_dim, half = dim / 2;
+    freqs.assign(half, 0.0f);
+    float freq_scale = 1.0f / c.rope_scale_factor;
+    if (!c.rope_yarn) {
+        for (int i = 0; i < half; i++) freqs[i] = freq_scale / powf(c.rope_freq_base, 2.0f * (float)i / (float)dim);
+        mscale = c.rope_attn_factor;
+        return;
+    }
+    float low, high;
+    if (c.yarn_beta_fast == 0.0f && c.yarn_beta_slow == 0.0f) {
+        low = 3.4028235e38f;
+        high = (float)dim / 2.0f - 1.0f;
+    } else {
+        const float PI = 3.14159265358979323846f;
+        float cf = (float)dim * logf((float)c.rope_orig_ctx / (c.yarn_beta_fast * 2.0f * PI)) /
+                   (2.0f * logf(c.rope_freq_base));
+        float cs = (float)dim * logf((float)c.rope_orig_ctx / (c.yarn_beta_slow * 2.0f * PI)) /
+                   (2.0f * logf(c.rope_freq_base));
+        low = fmaxf(0.0f, floorf(cf));
+        high = fminf((float)dim / 2.0f - 1.0f, ceilf(cs));
+    }
+    for (int i = 0; i < half; i++) {
+        float extrapolated = 1.0f / powf(c.rope_freq_base, 2.0f * (float)i / (float)dim);
+        float interpolated = freq_scale * extrapolated;
+        float y = ((float)i - low) / fmaxf(0.001f, high - low);
+        float cl = y < 0.0f ? 0.0f : (y > 1.0f ? 1.0f : y);
+        float mix = (1.0f - cl) * c.yarn_ext_factor;
+        float a = interpolated * (1.0f - mix);
+        float b = extrapolated * mix;
+        freqs[i] = a + b;
+    }
+    float factor = c.rope_scale_factor;
+    float m = c.yarn_mscale != 0.0f ? c.yarn_mscale : 1.0f;
+    float ratio = c.yarn_mscale_all_dim != 0.0f ? mscale_term(factor, m) / mscale_term(factor, c.yarn_mscale_all_dim)
+                                                : mscale_term(factor, 1.0f);
+    mscale = ratio * c.rope_attn_factor;
+}
+
+// ------------------------------------------------------------------ device
+
+struct Tensor {
+    DevWeight w;             // matrices (raw bytes + derived planes)
+    float *vec = nullptr;    // 1-D parameters widened to f32 (VectorParameter)
+    void *raw = nullptr;
+};
+
+template <class T>
+static void dev_alloc(T *&p, size_t count) {
+    void *v = nullptr;
+    SHIELD_CUDA(cudaMalloc(&v, std::max<size_t>(count, 1) * sizeof(T)));
+    p = static_cast<T *>(v);
+}
+template <class T>
+static void dev_free(T *&p) {
+    if (p) cudaFree((void *)p);
+    p = nullptr;
+}
+
+struct Buffers {
+    int64_t cap = 0;  // tokens
+    float *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ctx = nullptr, *g = nullptr, *u = nullptr;
+    int8_t *a8 = nullptr;
+    __half *a16 = nullptr;
+    float *da = nullptr, *ds = nullptr;
+    int32_t *sums = nullptr;
+    int32_t *meta = nullptr;   // ids | pos | tok_start | last  (4 * cap)
+    float *logits = nullptr;
+    int32_t *verdict = nullptr;
+    int32_t *err = nullptr;
+    int32_t *h_meta = nullptr;  // pinned
+    float *h_logits = nullptr;  // pinned
+    void free_all() {
+        dev_free(h); dev_free(q); dev_free(k); dev_free(v); dev_free(ctx); dev_free(g); dev_free(u);
+        dev_free(a8); dev_free(a16); dev_free(da); dev_free(ds); dev_free(sums); dev_free(meta);
+        dev_free(logits); dev_free(verdict); dev_free(err);
+        if (h_meta) cudaFreeHost(h_meta);
+        if (h_logits) cudaFreeHost(h_logits);
+        h_meta = nullptr;
+        h_logits = nullptr;
+        cap = 0;
+    }
+};
+
+struct Scratch {  // grow-on-demand buffers of the single-GEMM entry points
+    void *p = nullptr;
+    size_t bytes = 0;
+    void *get(size_t n) {
+        if (n > bytes) {
+            if (p) cudaFree(p);
+            p = nullptr;
+            bytes = 0;
+            SHIELD_CUDA(cudaMalloc(&p, n));
+            bytes = n;
+        }
+        return p;
+    }
+    ~Scratch() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct Device {
+    int ordinal = 0;
+    cudaStream_t stream = nullptr;
+    std::unordered_map<std::string, Tensor> tensors;
+    float *cos_t = nullptr, *sin_t = nullptr, *temp = nullptr;
+    Buffers buf;
+    Scratch sx, sy, sa, sd;
+    ~Device() {
+        cudaSetDevice(ordinal);
+        for (auto &kv : tensors) {
+            if (kv.second.raw) cudaFree(kv.second.raw);
+            if (kv.second.vec) cudaFree(kv.second.vec);
+            if (kv.second.w.scale_plane) cudaFree(kv.second.w.scale_plane);
+            if (kv.second.w.offset_plane) cudaFree(kv.second.w.offset_plane);
+        }
+        dev_free(cos_t);
+        dev_free(sin_t);
+        dev_free(temp);
+        buf.free_all();
+        if (stream) cudaStreamDestroy(stream);
+    }
+    const Tensor &get(const std::string &name) const {
+        auto it = tensors.find(name);
+        if (it == tensors.end()) throw Error(SHIELD_ERR_STATE, "tensor '" + name + "' has not been uploaded");
+        return it->second;
+    }
+};
+
+struct Ctx {
+    std::vector<std::unique_ptr<Device>> devs;
+    Config cfg;
+    bool configured = false;
+    int gemm_path = 0;
+};
+
+// -------------------------------------------------------------- operations
+
+static void check_launch(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw Error(SHIELD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, int64_t ldy, int epi) {
+    if (C.gemm_path != 1 && gemm_tc_supports(W.w, q.M)) {
+        cudaError_t e = launch_gemm_tc(W.w, q, y, ldy, epi, d.buf.err ? d.buf.err : nullptr, d.stream);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotSupported) check_launch(e, "tensor-core GEMM");
+    }
+    if (C.gemm_path == 2) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
+    check_launch(launch_gemm_simt(W.w, nullptr, W.w.rows, q, y, ldy, epi, d.stream), "CUDA-core GEMM");
+}
+
+static QAct qact(Buffers &b, int64_t M, int64_t K) {
+    QAct q;
+    q.a8 = b.a8;
+    q.a16 = b.a16;
+    q.da = b.da;
+    q.ds = b.ds;
+    q.sums = b.sums;
+    q.M = M;
+    q.K = K;
+    return q;
+}
+
+static void ensure_buffers(Ctx &C, Device &d) {
+    const Config &c = C.cfg;
+    int64_t T = c.max_batch_tokens;
+    if (d.buf.cap >= T) return;
+    d.buf.free_all();
+    int64_t K = c.max_k();
+    dev_alloc(d.buf.h, (size_t)(T * c.hidden));
+    dev_alloc(d.buf.q, (size_t)(T * c.qdim()));
+    dev_alloc(d.buf.k, (size_t)(T * c.kvdim()));
+    dev_alloc(d.buf.v, (size_t)(T * c.kvdim()));
+    dev_alloc(d.buf.ctx, (size_t)(T * c.qdim()));
+    dev_alloc(d.buf.g, (size_t)(T * c.ffn));
+    dev_alloc(d.buf.u, (size_t)(T * c.ffn));
+    dev_alloc(d.buf.a8, (size_t)(T * K));
+    dev_alloc(d.buf.a16, (size_t)(T * K));
+    dev_alloc(d.buf.da, (size_t)(T * K / 32));
+    dev_alloc(d.buf.ds, (size_t)(T * K / 32));
+    dev_alloc(d.buf.sums, (size_t)(T * K / 32));
+    dev_alloc(d.buf.meta, (size_t)(4 * T));
+    dev_alloc(d.buf.logits, (size_t)(T * 64));
+    dev_alloc(d.buf.verdict, 1024);
+    dev_alloc(d.buf.err, 1);
+    SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
+    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_meta, (size_t)(4 * T) * 4));
+    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_logits, (size_t)(T * 64) * 4));
+    d.buf.cap = T;
+}
+
+static void check_device_error(Device &d) {
+    int32_t e = 0;
+    SHIELD_CUDA(cudaMemcpyAsync(&e, d.buf.err, 4, cudaMemcpyDeviceToHost, d.stream));
+    SHIELD_CUDA(cudaStreamSynchronize(d.stream));
+    if (e) {
+        SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
+        if (e == 2) throw Error(SHIELD_ERR_RANGE, "a token id is outside the embedding table");
+        throw Error(SHIELD_ERR_TIMEOUT, "a device-side wait gave up (error word " + std::to_string(e) + ")");
+    }
+}
+
+struct Batch {  // one micro-batch of whole requests on one device
+    std::vector<int32_t> req;     // indices into the caller's request list
+    std::vector<int64_t> start;   // batch-local first token of each request
+    std::vector<int32_t> len;
+    int64_t tokens = 0;
+};
+
+// MinistralModel.ForwardAsync (MinistralModel.cs:183-271) over a packed
+// micro-batch: every request starts at position 0 with an empty cache.
+// Leaves verdict logits (R x nv) in d.buf.h_logits after a stream sync.
+static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batch &B, int nv,
+                          const volatile int32_t *cancel, int capture_layer, int capture_what, float *capture) {
+    const Config &c = C.cfg;
+    const int64_t M = B.tokens;
+    const int R = (int)B.req.size();
+    cudaStream_t s = d.stream;
+    Buffers &b = d.buf;
+    int32_t *hm = b.h_meta;
+    int32_t *h_ids = hm, *h_pos = hm + M, *h_start = hm + 2 * M, *h_last = hm + 3 * M;
+    for (int r = 0; r < R; r++) {
+        int64_t st = B.start[r];
+        for (int32_t p = 0; p < B.len[r]; p++) {
+            h_ids[st + p] = ids_host[st + p];
+            h_pos[st + p] = p;
+            h_start[st + p] = (int32_t)st;
+        }
+        h_last[r] = (int32_t)(st + B.len[r] - 1);
+    }
+    SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
+    const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_start = b.meta + 2 * M, *d_last = b.meta + 3 * M;
+    int max_len = *std::max_element(B.len.begin(), B.len.end());
+
+    const Tensor &emb = d.get("token_embd.weight");
+    check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
+    const float scale = 1.0f / sqrtf((float)c.head_dim);
+    auto cap = [&](int l, int what, const float *src, int64_t width) {
+        if (l == capture_layer && capture && capture_what == what)
+            SHIELD_CUDA(cudaMemcpyAsync(capture, src, (size_t)(M * width) * 4, cudaMemcpyDeviceToHost, s));
+    };
+    for (int l = 0; l < c.n_layers; l++) {
+        if (cancel && *cancel) {
+            cudaStreamSynchronize(s);
+            throw Error(SHIELD_ERR_CANCELLED, "cancelled");
+        }
+        std::string p = "blk." + std::to_string(l) + ".";
+        const Tensor &an = d.get(p + "attn_norm.weight"), &fn = d.get(p + "ffn_norm.weight");
+        const Tensor &wq = d.get(p + "attn_q.weight"), &wk = d.get(p + "attn_k.weight");
+        const Tensor &wv = d.get(p + "attn_v.weight"), &wo = d.get(p + "attn_output.weight");
+        const Tensor &wg = d.get(p + "ffn_gate.weight"), &wu = d.get(p + "ffn_up.weight");
+        const Tensor &wd = d.get(p + "ffn_down.weight");
+
+        QAct qa = qact(b, M, c.hidden);
+        bool want_norm = l == capture_layer && capture_what == SHIELD_ACT_ATTN_NORM;
+        check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, an.vec, c.eps, want_norm ? b.ctx : nullptr, qa, s),
+                     "attn norm");
+        cap(l, SHIELD_ACT_ATTN_NORM, b.ctx, c.hidden);
+        gemm(C, d, wq, qa, b.q, c.qdim(), EPI_STORE);
+        gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
+        gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
+        check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
+                                 d.temp, s), "rope q");
+        check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
+                                 nullptr, s), "rope k");
+        cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
+        cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
+        cap(l, SHIELD_ACT_V, b.v, c.kvdim());
+        check_launch(launch_attention(b.q, b.k, b.v, b.ctx, d_start, M, c.n_heads, c.n_kv_heads, c.head_dim, scale,
+                                      max_len, s), "attention");
+        cap(l, SHIELD_ACT_ATTN_WEIGHTED, b.ctx, c.qdim());
+        QAct qc = qact(b, M, c.qdim());
+        check_launch(launch_quantize(b.ctx, M, c.qdim(), c.qdim(), qc, s), "quantize context");
+        gemm(C, d, wo, qc, b.h, c.hidden, EPI_ADD);
+        cap(l, SHIELD_ACT_POST_ATTN, b.h, c.hidden);
+
+        check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, fn.vec, c.eps, nullptr, qa, s), "ffn norm");
+        gemm(C, d, wg, qa, b.g, c.ffn, EPI_STORE);
+        gemm(C, d, wu, qa, b.u, c.ffn, EPI_STORE);
+        check_launch(launch_swiglu(b.g, b.u, M * c.ffn, s), "swiglu");
+        QAct qf = qact(b, M, c.ffn);
+        check_launch(launch_quantize(b.g, M, c.ffn, c.ffn, qf, s), "quantize ffn");
+        gemm(C, d, wd, qf, b.h, c.hidden, EPI_ADD);
+        cap(l, SHIELD_ACT_OUTPUT, b.h, c.hidden);
+    }
+    if (nv > 0) {
+        // last position of every request -> final norm -> verdict rows of the tied head
+        const Tensor &on = d.get("output_norm.weight");
+        QAct qh = qact(b, R, c.hidden);
+        check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
+        check_launch(launch_gemm_simt(emb.w, b.verdict, nv, qh, b.logits, nv, EPI_STORE, s), "verdict head");
+        SHIELD_CUDA(cudaMemcpyAsync(b.h_logits, b.logits, (size_t)R * nv * 4, cudaMemcpyDeviceToHost, s));
+    }
+    check_device_error(d);
+}
+
+// ShieldstralModerator.Score (ShieldstralModerator.cs:348-364).
+static void score_one(const float *v, int n_yes, int n_no, float &score, float &yes, float &no) {
+    float y = -INFINITY, n = -INFINITY;
+    for (int i = 0; i < n_yes; i++)
+        if (v[i] > y) y = v[i];
+    for (int i = 0; i < n_no; i++)
+        if (v[n_yes + i] > n) n = v[n_yes + i];
+    float m = fmaxf(y, n);
+    float ey = expf(y - m), en = expf(n - m);
+    score = ey / (ey + en);
+    yes = y;
+    no = n;
+}
+
+static void upload_rope_tables(Ctx &C, Device &d) {
+    const Config &c = C.cfg;
+    int P = c.max_positions, half = c.rope_half;
+    std::vector<float> cs((size_t)P * half), sn((size_t)P * half), tp(P, 1.0f);
+    bool any_temp = false;
+    for (int p = 0; p < P; p++) {
+        for (int i = 0; i < half; i++) {
+            float theta = (float)p * c.freqs[i];
+            cs[(size_t)p * half + i] = cosf(theta) * c.mscale;
+            sn[(size_t)p * half + i] = sinf(theta) * c.mscale;
+        }
+        if (c.orig_ctx > 0 && c.temp_beta != 0.0f) {
+            float interval = floorf((float)p / (float)c.orig_ctx);
+            if (interval != 0.0f) {
+                float lg = logf(1.0f + interval);
+                float f = c.temp_beta * lg;
+                tp[p] = 1.0f + f;
+                any_temp = true;
+            }
+        }
+    }
+    SHIELD_CUDA(cudaSetDevice(d.ordinal));
+    dev_free(d.cos_t);
+    dev_free(d.sin_t);
+    dev_free(d.temp);
+    dev_alloc(d.cos_t, cs.size());
+    dev_alloc(d.sin_t, sn.size());
+    SHIELD_CUDA(cudaMemcpy(d.cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    SHIELD_CUDA(cudaMemcpy(d.sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    if (any_temp) {
+        dev_alloc(d.temp, tp.size());
+        SHIELD_CUDA(cudaMemcpy(d.temp, tp.data(), tp.size() * 4, cudaMemcpyHostToDevice));
+    }
+}
+
+static void set_config(Ctx &C, const shield_config *in) {
+    if (!in) throw Error(SHIELD_ERR_ARG, "config is null");
+    const shield_config &c = *in;
+    if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 || c.ffn <= 0 ||
+        c.vocab <= 0)
+        throw Error(SHIELD_ERR_ARG, "every model dimension must be positive");
+    if (c.n_heads % c.n_kv_heads)
+        throw Error(SHIELD_ERR_SHAPE, std::to_string(c.n_heads) + " attention heads do not divide into " +
+                                          std::to_string(c.n_kv_heads) + " KV heads");
+    if (c.hidden % 32 || c.ffn % 32 || (c.n_heads * c.head_dim) % 32)
+        throw Error(SHIELD_ERR_UNSUPPORTED, "hidden, ffn and q dimensions must be multiples of 32");
+    if (c.head_dim % 8 || c.head_dim > 256 || c.n_heads / c.n_kv_heads > 32)
+        throw Error(SHIELD_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 up to 256, and at most 32 query heads per KV head");
+    Config cfg;
+    cfg.n_layers = c.n_layers;
+    cfg.hidden = c.hidden;
+    cfg.n_heads = c.n_heads;
+    cfg.n_kv_heads = c.n_kv_heads;
+    cfg.head_dim = c.head_dim;
+    cfg.ffn = c.ffn;
+    cfg.vocab = c.vocab;
+    cfg.eps = c.rms_eps;
+    if (c.n_rope_freqs > 0) {
+        if (!c.rope_freqs || c.n_rope_freqs * 2 > c.head_dim) throw Error(SHIELD_ERR_ARG, "bad rope frequency table");
+        cfg.freqs.assign(c.rope_freqs, c.rope_freqs + c.n_rope_freqs);
+        cfg.mscale = c.rope_mscale;
+    } else {
+        if (c.rope_dim <= 0 || c.rope_dim > c.head_dim || c.rope_dim % 2)
+            throw Error(SHIELD_ERR_ARG, "rope_dim must be even and at most head_dim");
+        rope_freqs(c, cfg.freqs, cfg.mscale);
+    }
+    cfg.rope_half = (int)cfg.freqs.size();
+    cfg.temp_beta = c.attn_temperature_beta;
+    cfg.orig_ctx = c.rope_orig_ctx;
+    cfg.max_positions = c.max_positions > 0 ? c.max_positions : 8192;
+    cfg.max_batch_tokens = c.max_batch_tokens > 0 ? c.max_batch_tokens : 16384;
+    int group = c.n_heads / c.n_kv_heads;
+    int64_t att_smem = (int64_t)group * c.head_dim * 4 + (int64_t)group * cfg.max_positions * 4;
+    if (att_smem > 227 * 1024)
+        throw Error(SHIELD_ERR_UNSUPPORTED, "max_positions too long for the attention kernel's score buffer");
+    if (cfg.max_batch_tokens < cfg.max_positions) cfg.max_batch_tokens = cfg.max_positions;
+    C.cfg = cfg;
+    C.configured = true;
+    for (auto &d : C.devs) {
+        upload_rope_tables(C, *d);
+        d->buf.free_all();
+    }
+}
+
+static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_t cols, const void *bytes,
+                   size_t nbytes) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "shield_set_config must come before uploads");
+    if (!name || !bytes) throw Error(SHIELD_ERR_ARG, "name and bytes must be non-null");
+    if (rows <= 0 || cols <= 0) throw Error(SHIELD_ERR_ARG, "rows and cols must be positive");
+    int64_t rb = row_bytes_of((int)type, cols);
+    if (rb < 0) throw Error(SHIELD_ERR_UNSUPPORTED, std::string(name) + ": type " + std::to_string(type) +
+                                                         " has no kernel, or cols is not a multiple of 32");
+    if ((size_t)(rb * rows) != nbytes)
+        throw Error(SHIELD_ERR_ARG, std::string(name) + ": expected " + std::to_string(rb * rows) + " bytes, got " +
+                                        std::to_string(nbytes));
+    std::string n(name);
+    bool is_vector = n.size() > 11 && n.compare(n.size() - 11, 11, "norm.weight") == 0;
+    const Config &c = C.cfg;
+    if (n == "token_embd.weight" && (cols != c.hidden || rows != c.vocab))
+        throw Error(SHIELD_ERR_SHAPE, "token_embd is " + std::to_string(rows) + "x" + std::to_string(cols) +
+                                          " but the model is vocab " + std::to_string(c.vocab) + " x hidden " +
+                                          std::to_string(c.hidden));
+    if (is_vector && rows * cols != c.hidden) throw Error(SHIELD_ERR_SHAPE, n + " must have hidden elements");
+    if (!is_vector && (type == T_F32 || type == T_F16))
+        throw Error(SHIELD_ERR_UNSUPPORTED, n + ": float matrices are outside the integer path");
+    for (auto &dp : C.devs) {
+        Device &d = *dp;
+        SHIELD_CUDA(cudaSetDevice(d.ordinal));
+        auto old = d.tensors.find(n);
+        if (old != d.tensors.end()) {
+            if (old->second.raw) cudaFree(old->second.raw);
+            if (old->second.vec) cudaFree(old->second.vec);
+            if (old->second.w.scale_plane) cudaFree(old->second.w.scale_plane);
+            if (old->second.w.offset_plane) cudaFree(old->second.w.offset_plane);
+            d.tensors.erase(old);
+        }
+        Tensor t;
+        if (is_vector) {
+            std::vector<float> f((size_t)(rows * cols));
+            if (type == T_F32) {
+                memcpy(f.data(), bytes, f.size() * 4);
+            } else {
+                const uint16_t *hsrc = static_cast<const uint16_t *>(bytes);
+                for (size_t i = 0; i < f.size(); i++) {
+                    __half_raw r;
+                    r.x = hsrc[i];
+                    f[i] = __half2float(__half(r));
+                }
+            }
+            dev_alloc(t.vec, f.size());
+            SHIELD_CUDA(cudaMemcpy(t.vec, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
+        } else {
+            SHIELD_CUDA(cudaMalloc(&t.raw, nbytes + 64));
+            SHIELD_CUDA(cudaMemcpy(t.raw, bytes, nbytes, cudaMemcpyHostToDevice));
+            t.w.type = (int)type;
+            t.w.rows = rows;
+            t.w.cols = cols;
+            t.w.row_bytes = rb;
+            t.w.data = static_cast<const uint8_t *>(t.raw);
+            dev_alloc(t.w.scale_plane, (size_t)(rows * (cols / 32)));
+            if (type == T_Q4_1 || type == T_Q5_1) dev_alloc(t.w.offset_plane, (size_t)(rows * (cols / 32)));
+            check_launch(launch_build_planes(t.w, nullptr), "scale planes");
+            SHIELD_CUDA(cudaDeviceSynchronize());
+        }
+        d.tensors.emplace(n, t);
+    }
+}
+
+static void validate_ids(const Ctx &C, const int32_t *ids, int64_t n) {
+    for (int64_t i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= C.cfg.vocab)
+            throw Error(SHIELD_ERR_RANGE, "token id " + std::to_string(ids[i]) + " is outside the " +
+                                              std::to_string(C.cfg.vocab) + "-entry embedding table");
+}
+
+// Packs a device's requests (in the given order) into micro-batches.
+static std::vector<Batch> make_batches(const Ctx &C, const std::vector<int32_t> &reqs, const int64_t *offsets) {
+    std::vector<Batch> out;
+    Batch cur;
+    for (int32_t r : reqs) {
+        int32_t len = (int32_t)(offsets[r + 1] - offsets[r]);
+        if (cur.tokens + len > C.cfg.max_batch_tokens && !cur.req.empty()) {
+            out.push_back(cur);
+            cur = Batch();
+        }
+        cur.req.push_back(r);
+        cur.start.push_back(cur.tokens);
+        cur.len.push_back(len);
+        cur.tokens += len;
+    }
+    if (!cur.req.empty()) out.push_back(cur);
+    return out;
+}
+
+static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int32_t n_req, const int32_t *verdict,
+                        int32_t n_yes, int32_t n_no, float *yes, float *no, float *score, float *logits,
+                        const volatile int32_t *cancel) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (n_req < 0 || (n_req > 0 && (!ids || !offsets || !yes || !no || !score)))
+        throw Error(SHIELD_ERR_ARG, "null buffer");
+    if (n_yes <= 0 || n_no <= 0 || !verdict) throw Error(SHIELD_ERR_ARG, "need at least one yes and one no id");
+    int nv = n_yes + n_no;
+    if (nv > 64) throw Error(SHIELD_ERR_ARG, "at most 64 verdict ids");
+    for (int i = 0; i < nv; i++)
+        if (verdict[i] < 0 || verdict[i] >= C.cfg.vocab)
+            throw Error(SHIELD_ERR_RANGE, "verdict id " + std::to_string(verdict[i]) + " is outside the vocabulary");
+    if (n_req == 0) return;
+    if (offsets[0] != 0) throw Error(SHIELD_ERR_ARG, "offsets[0] must be 0");
+    std::vector<std::pair<double, int32_t>> cost(n_req);
+    for (int32_t r = 0; r < n_req; r++) {
+        int64_t len = offsets[r + 1] - offsets[r];
+        if (len <= 0) throw Error(SHIELD_ERR_ARG, "request " + std::to_string(r) + " has no tokens");
+        if (len > C.cfg.max_positions)
+            throw Error(SHIELD_ERR_RANGE, "request " + std::to_string(r) + " has " + std::to_string(len) +
+                                              " tokens, more than max_positions " +
+                                              std::to_string(C.cfg.max_positions));
+        cost[r] = {(double)len * (1.0 + (double)len / 8192.0), r};
+    }
+    validate_ids(C, ids, offsets[n_req]);
+    // longest-processing-time-first assignment of requests to GPUs
+    int D = (int)C.devs.size();
+    std::vector<std::vector<int32_t>> assign(D);
+    if (D == 1) {
+        assign[0].resize(n_req);
+        std::iota(assign[0].begin(), assign[0].end(), 0);
+    } else {
+        std::vector<std::pair<double, int32_t>> sorted = cost;
+        std::sort(sorted.begin(), sorted.end(), [](auto &a, auto &b) { return a.first > b.first; });
+        std::vector<double> load(D, 0.0);
+        for (auto &cr : sorted) {
+            int best = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+            load[best] += cr.first;
+            assign[best].push_back(cr.second);
+        }
+        for (auto &a : assign) std::sort(a.begin(), a.end());
+    }
+    std::vector<std::string> errors(D);
+    std::vector<shield_status> codes(D, SHIELD_OK);
+    auto run = [&](int di) {
+        try {
+            Device &d = *C.devs[di];
+            SHIELD_CUDA(cudaSetDevice(d.ordinal));
+            ensure_buffers(C, d);
+            SHIELD_CUDA(cudaMemcpyAsync(d.buf.verdict, verdict, (size_t)nv * 4, cudaMemcpyHostToDevice, d.stream));
+            std::vector<int32_t> packed;
+            for (const Batch &B : make_batches(C, assign[di], offsets)) {
+                packed.resize(B.tokens);
+                for (size_t i = 0; i < B.req.size(); i++)
+                    memcpy(packed.data() + B.start[i], ids + offsets[B.req[i]], (size_t)B.len[i] * 4);
+                forward_batch(C, d, packed.data(), B, nv, cancel, -1, 0, nullptr);
+                for (size_t i = 0; i < B.req.size(); i++) {
+                    int32_t r = B.req[i];
+                    const float *v = d.buf.h_logits + i * nv;
+                    score_one(v, n_yes, n_no, score[r], yes[r], no[r]);
+                    if (logits) memcpy(logits + (int64_t)r * nv, v, (size_t)nv * 4);
+                }
+            }
+        } catch (const Error &e) {
+            codes[di] = e.code;
+            errors[di] = e.what();
+        } catch (const std::exception &e) {
+            codes[di] = SHIELD_ERR_CUDA;
+            errors[di] = e.what();
+        }
+    };
+    if (D == 1) {
+        run(0);
+    } else {
+        std::vector<std::thread> th;
+        for (int di = 0; di < D; di++) th.emplace_back(run, di);
+        for (auto &t : th) t.join();
+    }
+    for (int di = 0; di < D; di++)
+        if (codes[di] != SHIELD_OK) throw Error(codes[di], errors[di]);
+}
+
+static Device &device_of(Ctx &C, int32_t device) {
+    if (device < 0 || device >= (int32_t)C.devs.size())
+        throw Error(SHIELD_ERR_RANGE, "device index " + std::to_string(device) + " is outside the context");
+    Device &d = *C.devs[device];
+    SHIELD_CUDA(cudaSetDevice(d.ordinal));
+    return d;
+}
+
+static QAct scratch_qact(Device &d, int64_t M, int64_t K) {
+    size_t n = (size_t)(M * K);
+    size_t nb = (size_t)(M * K / 32);
+    char *base = static_cast<char *>(d.sa.get(n * 3 + nb * 12 + 1024));
+    QAct q;
+    q.a8 = reinterpret_cast<int8_t *>(base);
+    q.a16 = reinterpret_cast<__half *>(base + ((n + 255) & ~size_t(255)));
+    char *sp = base + ((n + 255) & ~size_t(255)) + ((2 * n + 255) & ~size_t(255));
+    q.da = reinterpret_cast<float *>(sp);
+    q.ds = q.da + nb;
+    q.sums = reinterpret_cast<int32_t *>(q.ds + nb);
+    q.M = M;
+    q.K = K;
+    return q;
+}
+
+static void qmatmul_dev(Ctx &C, Device &d, const Tensor &W, const float *d_x, int64_t M, float *d_y,
+                        const int32_t *d_rows, int32_t n_rows) {
+    QAct q = scratch_qact(d, M, W.w.cols);
+    check_launch(launch_quantize(d_x, M, W.w.cols, W.w.cols, q, d.stream), "quantize");
+    if (d_rows) {
+        check_launch(launch_gemm_simt(W.w, d_rows, n_rows, q, d_y, n_rows, EPI_STORE, d.stream), "row-subset GEMM");
+    } else {
+        if (!d.buf.err) {
+            dev_alloc(d.buf.err, 1);
+            SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
+        }
+        gemm(C, d, W, q, d_y, W.w.rows, EPI_STORE);
+    }
+}
+
+static const Tensor &matrix(Device &d, const char *weight) {
+    if (!weight) throw Error(SHIELD_ERR_ARG, "weight name is null");
+    const Tensor &W = d.get(weight);
+    if (!W.raw) throw Error(SHIELD_ERR_ARG, std::string(weight) + " is a vector, not a matrix");
+    return W;
+}
+
+}  // namespace shield
+
+using namespace shield;
+
+struct shield_ctx {
+    Ctx c;
+};
+
+template <class F>
+static shield_status guarded(F &&f) {
+    try {
+        f();
+        g_last_error.clear();
+        return SHIELD_OK;
+    } catch (const Error &e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        g_last_error = "host memory exhausted";
+        return SHIELD_ERR_NOMEM;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return SHIELD_ERR_CUDA;
+    }
+}
+
+extern "C" {
+
+shield_status shield_open(int32_t device_mask, shield_ctx **out) {
+    return guarded([&] {
+        if (!out) throw Error(SHIELD_ERR_ARG, "out is null");
+        *out = nullptr;
+        int n = 0;
+        SHIELD_CUDA(cudaGetDeviceCount(&n));
+        if (device_mask == 0) device_mask = 1;
+        auto ctx = std::make_unique<shield_ctx>();
+        for (int i = 0; i < 31; i++) {
+            if (!(device_mask & (1 << i))) continue;
+            if (i >= n) throw Error(SHIELD_ERR_RANGE, "device " + std::to_string(i) + " does not exist");
+            auto d = std::make_unique<Device>();
+            d->ordinal = i;
+            SHIELD_CUDA(cudaSetDevice(i));
+            SHIELD_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+            ctx->c.devs.push_back(std::move(d));
+        }
+        *out = ctx.release();
+    });
+}
+
+void shield_close(shield_ctx *ctx) {
+    if (!ctx) return;
+    for (auto &d : ctx->c.devs) {
+        cudaSetDevice(d->ordinal);
+        cudaStreamSynchronize(d->stream);
+    }
+    delete ctx;
+}
+
+int32_t shield_device_count(const shield_ctx *ctx) { return ctx ? (int32_t)ctx->c.devs.size() : 0; }
+
+shield_status shield_set_config(shield_ctx *ctx, const shield_config *cfg) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        set_config(ctx->c, cfg);
+    });
+}
+
+shield_status shield_upload_tensor(shield_ctx *ctx, const char *name, uint32_t ggml_type, int64_t rows, int64_t cols,
+                                   const void *bytes, size_t nbytes) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        upload(ctx->c, name, ggml_type, rows, cols, bytes, nbytes);
+    });
+}
+
+shield_status shield_score_batch(shield_ctx *ctx, const int32_t *ids, const int64_t *offsets, int32_t n_req,
+                                 const int32_t *verdict_ids, int32_t n_yes, int32_t n_no, float *yes, float *no,
+                                 float *score, float *logits, const volatile int32_t *cancel) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        score_batch(ctx->c, ids, offsets, n_req, verdict_ids, n_yes, n_no, yes, no, score, logits, cancel);
+    });
+}
+
+shield_status shield_qmatmul(shield_ctx *ctx, int32_t device, const char *weight, const float *x, int64_t M,
+                             float *y, const int32_t *row_ids, int32_t n_rows) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        Ctx &C = ctx->c;
+        Device &d = device_of(C, device);
+        const Tensor &W = matrix(d, weight);
+        int64_t n_out = row_ids ? n_rows : W.w.rows;
+        if (M < 0 || (row_ids && n_rows < 0)) throw Error(SHIELD_ERR_ARG, "negative size");
+        if (row_ids)
+            for (int32_t i = 0; i < n_rows; i++)
+                if (row_ids[i] < 0 || row_ids[i] >= W.w.rows)
+                    throw Error(SHIELD_ERR_RANGE, "Row " + std::to_string(row_ids[i]) + " is outside the matrix's " +
+                                                      std::to_string(W.w.rows) + " rows.");
+        if (M == 0 || n_out == 0) return;
+        if (!x || !y) throw Error(SHIELD_ERR_ARG, "x and y must be non-null");
+        float *dx = static_cast<float *>(d.sx.get((size_t)(M * W.w.cols) * 4));
+        float *dy = static_cast<float *>(d.sy.get((size_t)(M * n_out) * 4));
+        int32_t *drows = nullptr;
+        if (row_ids) {
+            drows = static_cast<int32_t *>(d.sd.get((size_t)n_rows * 4));
+            SHIELD_CUDA(cudaMemcpyAsync(drows, row_ids, (size_t)n_rows * 4, cudaMemcpyHostToDevice, d.stream));
+        }
+        SHIELD_CUDA(cudaMemcpyAsync(dx, x, (size_t)(M * W.w.cols) * 4, cudaMemcpyHostToDevice, d.stream));
+        qmatmul_dev(C, d, W, dx, M, dy, drows, n_rows);
+        SHIELD_CUDA(cudaMemcpyAsync(y, dy, (size_t)(M * n_out) * 4, cudaMemcpyDeviceToHost, d.stream));
+        check_device_error(d);
+    });
+}
+
+shield_status shield_qmatmul_device(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x, int64_t M,
+                                    float *d_y) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        Ctx &C = ctx->c;
+        Device &d = device_of(C, device);
+        const Tensor &W = matrix(d, weight);
+        if (M < 0) throw Error(SHIELD_ERR_ARG, "negative size");
+        if (M == 0) return;
+        if (!d_x || !d_y) throw Error(SHIELD_ERR_ARG, "x and y must be non-null");
+        qmatmul_dev(C, d, W, d_x, M, d_y, nullptr, 0);
+    });
+}
+
+shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const char *weight, const float *x, int64_t M,
+                                      int32_t *dots, int32_t path) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        Ctx &C = ctx->c;
+        Device &d = device_of(C, device);
+        const Tensor &W = matrix(d, weight);
+        if (M <= 0 || !x || !dots) throw Error(SHIELD_ERR_ARG, "bad arguments");
+        int64_t nb = W.w.cols / 32;
+        float *dx = static_cast<float *>(d.sx.get((size_t)(M * W.w.cols) * 4));
+        int32_t *dd = static_cast<int32_t *>(d.sy.get((size_t)(M * W.w.rows * nb) * 4));
+        SHIELD_CUDA(cudaMemcpyAsync(dx, x, (size_t)(M * W.w.cols) * 4, cudaMemcpyHostToDevice, d.stream));
+        QAct q = scratch_qact(d, M, W.w.cols);
+        check_launch(launch_quantize(dx, M, W.w.cols, W.w.cols, q, d.stream), "quantize");
+        if (!d.buf.err) {
+            dev_alloc(d.buf.err, 1);
+            SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
+        }
+        bool tc = path == 2 || (path == 0 && C.gemm_path != 1 && gemm_tc_supports(W.w, M));
+        if (tc) {
+            cudaError_t e = launch_block_dots_tc(W.w, q, dd, d.buf.err, d.stream);
+            if (e == cudaErrorNotSupported) throw Error(SHIELD_ERR_UNSUPPORTED, "tensor-core path does not take this shape");
+            check_launch(e, "tensor-core block dots");
+        } else {
+            check_launch(launch_block_dots(W.w, q, dd, d.stream), "block dots");
+        }
+        SHIELD_CUDA(cudaMemcpyAsync(dots, dd, (size_t)(M * W.w.rows * nb) * 4, cudaMemcpyDeviceToHost, d.stream));
+        check_device_error(d);
+    });
+}
+
+shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        if (path < 0 || path > 2) throw Error(SHIELD_ERR_ARG, "path must be 0, 1 or 2");
+        ctx->c.gemm_path = path;
+    });
+}
+
+shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int32_t *ids, int32_t n, int32_t layer,
+                                      int32_t what, float *out) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        Ctx &C = ctx->c;
+        if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+        Device &d = device_of(C, device);
+        if (n <= 0 || !ids || !out) throw Error(SHIELD_ERR_ARG, "bad arguments");
+        if (n > C.cfg.max_positions) throw Error(SHIELD_ERR_RANGE, "request longer than max_positions");
+        if (layer < 0 || layer >= C.cfg.n_layers) throw Error(SHIELD_ERR_RANGE, "layer out of range");
+        if (what < SHIELD_ACT_OUTPUT || what > SHIELD_ACT_ATTN_NORM) throw Error(SHIELD_ERR_ARG, "unknown activation");
+        validate_ids(C, ids, n);
+        ensure_buffers(C, d);
+        Batch B;
+        B.req = {0};
+        B.start = {0};
+        B.len = {n};
+        B.tokens = n;
+        forward_batch(C, d, ids, B, 0, nullptr, layer, what, out);
+    });
+}
+
+shield_status shield_device_stream(shield_ctx *ctx, int32_t device, void **stream) {
+    return guarded([&] {
+        if (!ctx || !stream) throw Error(SHIELD_ERR_ARG, "null argument");
+        *stream = (void *)device_of(ctx->c, device).stream;
+    });
+}
+
+const char *shield_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"

@@ -1,0 +1,176 @@
+// Exact integer GEMM on CUDA cores: y[t, n] over weight rows n (or a subset),
+// with the reference's per-output arithmetic (IntegerGemm.cs:371-457):
+//   i = Σ_k w_k·a_k                      (= -z·Σa + Σ u·a, exact int32)
+//   f = fma(float(i), d_w·d_a, f)         block by block, in order
+//   f = fma(m_w, d_a·float(Σa), f)        Q4_1 / Q5_1 only
+// Used for small token counts, row subsets (the verdict head) and any K that
+// the tensor-core kernel does not take. Bit-identical to that kernel.
+#include "common.cuh"
+#include "ops.h"
+
+namespace shield {
+
+constexpr int SIMT_ROWS = 64;    // weight rows per CTA
+constexpr int SIMT_TOKENS = 32;  // tokens per CTA
+constexpr int SIMT_THREADS = 128;
+
+template <int TYPE, int EPI>
+__global__ void __launch_bounds__(SIMT_THREADS)
+k_gemm_simt(const uint8_t *__restrict__ W, int64_t w_rows, int64_t row_bytes, const int32_t *__restrict__ row_ids,
+            int64_t n_out, int64_t K, const int8_t *__restrict__ A, const float *__restrict__ da,
+            const float *__restrict__ ds, int64_t M, float *__restrict__ Y, int64_t ldy) {
+    constexpr int BB = block_bytes(TYPE);
+    constexpr bool OFF = has_offset(TYPE);
+    __shared__ int32_t ws[SIMT_ROWS][9];     // 32 signed weights as 8 packed words (+1 pad)
+    __shared__ float wsc[SIMT_ROWS], woff[SIMT_ROWS];
+    __shared__ int32_t as_[SIMT_TOKENS][9];
+    __shared__ float ad[SIMT_TOKENS], ads[SIMT_TOKENS];
+
+    const int tid = threadIdx.x;
+    const int64_t n0 = (int64_t)blockIdx.x * SIMT_ROWS;
+    const int64_t t0 = (int64_t)blockIdx.y * SIMT_TOKENS;
+    const int tr = tid % 16, tt = tid / 16;  // 4 rows x 4 tokens per thread
+    const int64_t nb = K / 32;
+
+    // the weight row this thread unpacks half of
+    const int lr = tid / 2, half = tid % 2;
+    const int64_t out_row = n0 + lr;
+    const bool row_ok = out_row < n_out;
+    const int64_t src_row = row_ok ? (row_ids ? (int64_t)row_ids[out_row] : out_row) : 0;
+    const uint8_t *wrow = W + src_row * row_bytes;
+    const int lt = tid / 4, part = tid % 4;  // token this thread loads a quarter of
+    const bool tok_ok = t0 + lt < M;
+
+    float f[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) f[i][j] = 0.0f;
+
+    for (int64_t b = 0; b < nb; b++) {
+        // -- weights: 16 signed values per thread, packed 4 per word
+        {
+            const uint8_t *blk = wrow + b * BB;
+            int32_t words[4];
+#pragma unroll
+            for (int wi = 0; wi < 4; wi++) {
+                uint32_t packed = 0;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    int j = half * 16 + wi * 4 + k;
+                    int v = row_ok ? weight_at<TYPE>(blk, j) : 0;
+                    packed |= (uint32_t)(v & 0xFF) << (8 * k);
+                }
+                words[wi] = (int32_t)packed;
+            }
+#pragma unroll
+            for (int wi = 0; wi < 4; wi++) ws[lr][half * 4 + wi] = words[wi];
+            if (half == 0) {
+                wsc[lr] = row_ok ? h2f(ld_u16(blk)) : 0.0f;
+                if (OFF) woff[lr] = row_ok ? h2f(ld_u16(blk + 2)) : 0.0f;
+            }
+        }
+        // -- activations: 8 bytes per thread
+        {
+            int2 v = make_int2(0, 0);
+            if (tok_ok) v = *reinterpret_cast<const int2 *>(A + (t0 + lt) * K + b * 32 + part * 8);
+            as_[lt][part * 2] = v.x;
+            as_[lt][part * 2 + 1] = v.y;
+            if (part == 0) {
+                ad[lt] = tok_ok ? da[(t0 + lt) * nb + b] : 0.0f;
+                if (OFF) ads[lt] = tok_ok ? ds[(t0 + lt) * nb + b] : 0.0f;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = tr * 4 + i;
+            const float sw = wsc[r];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int t = tt * 4 + j;
+                int acc = 0;
+#pragma unroll
+                for (int k = 0; k < 8; k++) acc = __dp4a(ws[r][k], as_[t][k], acc);
+                f[i][j] = __fmaf_rn((float)acc, __fmul_rn(sw, ad[t]), f[i][j]);
+                if (OFF) f[i][j] = __fmaf_rn(woff[r], ads[t], f[i][j]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int64_t n = n0 + tr * 4 + i;
+        if (n >= n_out) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int64_t t = t0 + tt * 4 + j;
+            if (t >= M) continue;
+            float *dst = Y + t * ldy + n;
+            if (EPI == EPI_ADD)
+                *dst = __fadd_rn(*dst, f[i][j]);
+            else
+                *dst = f[i][j];
+        }
+    }
+}
+
+template <int TYPE>
+static void gemm_simt_t(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                        int64_t ldy, int epi, cudaStream_t s) {
+    dim3 grid((unsigned)((n_out + SIMT_ROWS - 1) / SIMT_ROWS), (unsigned)((q.M + SIMT_TOKENS - 1) / SIMT_TOKENS));
+    if (epi == EPI_ADD)
+        k_gemm_simt<TYPE, EPI_ADD><<<grid, SIMT_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, row_ids, n_out,
+                                                                  w.cols, q.a8, q.da, q.ds, q.M, y, ldy);
+    else
+        k_gemm_simt<TYPE, EPI_STORE><<<grid, SIMT_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, row_ids, n_out,
+                                                                    w.cols, q.a8, q.da, q.ds, q.M, y, ldy);
+}
+
+cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                             int64_t ldy, int epi, cudaStream_t s) {
+    if (n_out == 0 || q.M == 0) return cudaSuccess;
+    if (w.cols % 32 || !q.a8) return cudaErrorInvalidValue;
+    if (q.M > 65535LL * SIMT_TOKENS) return cudaErrorInvalidValue;
+    switch (w.type) {
+    case T_Q4_0: gemm_simt_t<T_Q4_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q4_1: gemm_simt_t<T_Q4_1>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q5_0: gemm_simt_t<T_Q5_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q5_1: gemm_simt_t<T_Q5_1>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q8_0: gemm_simt_t<T_Q8_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    default: return cudaErrorNotSupported;
+    }
+    return cudaGetLastError();
+}
+
+// Raw per-block dots: one thread per (t, n, b).
+template <int TYPE>
+__global__ void k_block_dots(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
+                             const int8_t *__restrict__ A, int64_t M, int32_t *__restrict__ dots) {
+    int64_t nb = K / 32;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M * rows * nb) return;
+    int64_t b = i % nb, n = (i / nb) % rows, t = i / (nb * rows);
+    const uint8_t *blk = W + n * row_bytes + b * block_bytes(TYPE);
+    const int8_t *a = A + t * K + b * 32;
+    int acc = 0;
+    for (int j = 0; j < 32; j++) acc += weight_at<TYPE>(blk, j) * (int)a[j];
+    dots[i] = acc;
+}
+
+cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s) {
+    int64_t n = q.M * w.rows * (w.cols / 32);
+    if (n == 0) return cudaSuccess;
+    unsigned g = (unsigned)((n + 255) / 256);
+    switch (w.type) {
+    case T_Q4_0: k_block_dots<T_Q4_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.M, dots); break;
+    case T_Q4_1: k_block_dots<T_Q4_1><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.M, dots); break;
+    case T_Q5_0: k_block_dots<T_Q5_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.M, dots); break;
+    case T_Q5_1: k_block_dots<T_Q5_1><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.M, dots); break;
+    case T_Q8_0: k_block_dots<T_Q8_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.M, dots); break;
+    default: return cudaErrorNotSupported;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace shield

@@ -1,0 +1,75 @@
+// Host-side launchers of the Shieldstral kernels. Every launcher is
+// asynchronous on the given stream and does no allocation.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace shield {
+
+// GGML type ids (reference Gguf/GgmlType.cs:10-44).
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8 };
+
+// Bytes per 32-weight block (GgmlType.cs:78-82); 0 when the type has no integer kernel.
+inline constexpr int block_bytes_host(int type) {
+    return type == T_Q4_0 ? 18 : type == T_Q4_1 ? 20 : type == T_Q5_0 ? 22 : type == T_Q5_1 ? 24 : type == T_Q8_0 ? 34 : 0;
+}
+
+// Quantized activations, row-major M x K (IntegerGemm.QuantizeActivations
+// output, IntegerGemm.cs:97-138): int8 values (and the same integers as f16
+// for the tensor-core path), one f32 scale d per 32-block, the block's Σq,
+// and ds = d * float(Σq), the multiplier of the Q4_1/Q5_1 offsets
+// (IntegerGemm.cs:405-411).
+struct QAct {
+    int8_t *a8 = nullptr;
+    __half *a16 = nullptr;
+    float *da = nullptr;
+    float *ds = nullptr;
+    int32_t *sums = nullptr;
+    int64_t M = 0, K = 0;
+};
+
+// A weight matrix resident on one device: the GGUF bytes unchanged, rows =
+// output features, each row K/32 contiguous blocks (WeightMatrix.cs:16-40),
+// plus planes derived once at upload: the f16 block scales (and offsets)
+// widened to f32, stored block-major [K/32][rows].
+struct DevWeight {
+    int type = 0;
+    int64_t rows = 0, cols = 0, row_bytes = 0;
+    const uint8_t *data = nullptr;
+    float *scale_plane = nullptr;
+    float *offset_plane = nullptr;
+};
+
+enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1 };
+
+cudaError_t launch_quantize(const float *x, int64_t M, int64_t K, int64_t ldx, const QAct &q, cudaStream_t s);
+// RMSNorm (Kernels.cs:26-61) fused with the activation quantizer; rows are
+// optionally gathered (row_idx) and the normalized floats optionally kept (y).
+cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
+                                 float eps, float *y, const QAct &q, cudaStream_t s);
+cudaError_t launch_embed(const DevWeight &emb, const int32_t *ids, int64_t M, float *h, int32_t *err,
+                         cudaStream_t s);
+cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s);
+
+// Exact integer GEMM on CUDA cores; any K % 32 == 0, optional row subset.
+cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                             int64_t ldy, int epi, cudaStream_t s);
+// tcgen05 tensor-core GEMM; K % 256 == 0, full row range. Returns
+// cudaErrorNotSupported for shapes it does not take.
+cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
+                           cudaStream_t s);
+bool gemm_tc_supports(const DevWeight &w, int64_t M);
+// Per-block int32 dots (t, n, b) for the bit-exactness check.
+cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s);
+cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s);
+
+cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
+                        const float *cos_t, const float *sin_t, int half, const float *temp, cudaStream_t s);
+cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, const int32_t *tok_start,
+                             int64_t M, int n_heads, int n_kv_heads, int head_dim, float scale, int max_len,
+                             cudaStream_t s);
+cudaError_t launch_swiglu(float *g, float *u, int64_t n, cudaStream_t s);
+
+}  // namespace shield

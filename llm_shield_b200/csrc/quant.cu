@@ -1,0 +1,172 @@
+// Activation quantization, fused RMSNorm + quantization, embedding gather,
+// and the one-time derived scale planes of an uploaded weight.
+#include "common.cuh"
+#include "ops.h"
+
+namespace shield {
+
+// One warp per 32-block: lane j owns element j (IntegerGemm.cs:97-138).
+__global__ void k_quantize(const float *__restrict__ x, int64_t M, int64_t K, int64_t ldx, QAct q) {
+    int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    int64_t nb = K / 32;
+    if (warp >= M * nb) return;
+    int64_t t = warp / nb, b = warp % nb;
+    float v = x[t * ldx + b * 32 + lane];
+    float d;
+    int sum;
+    int qv = quantize_lane(v, d, sum);
+    int64_t o = t * K + b * 32 + lane;
+    if (q.a8) q.a8[o] = (int8_t)qv;
+    if (q.a16) q.a16[o] = __int2half_rn(qv);
+    if (lane == 0) {
+        int64_t so = t * nb + b;
+        q.da[so] = d;
+        if (q.ds) q.ds[so] = __fmul_rn(d, (float)sum);
+        if (q.sums) q.sums[so] = sum;
+    }
+}
+
+cudaError_t launch_quantize(const float *x, int64_t M, int64_t K, int64_t ldx, const QAct &q, cudaStream_t s) {
+    int64_t warps = M * (K / 32);
+    if (warps == 0) return cudaSuccess;
+    int threads = 256;
+    int64_t blocks = (warps * 32 + threads - 1) / threads;
+    k_quantize<<<(unsigned)blocks, threads, 0, s>>>(x, M, K, ldx, q);
+    return cudaGetLastError();
+}
+
+// Kernels.RmsNorm (Kernels.cs:26-61) in the oracle's operation order:
+// 16 lanes (two 8-wide vectors) of x*x then +, each a sequential chain over
+// the row; Vector.Sum of each vector; the sum widened to double; the tail in
+// double; scale = 1/sqrt((float)(sum/n) + eps); y = (x*scale)*w. Then every
+// 32-block of y is quantized like k_quantize. One CTA of 128 threads per row.
+__global__ void k_rmsnorm_quant(const float *__restrict__ x, const int32_t *__restrict__ row_idx, int K,
+                                const float *__restrict__ w, float eps, float *__restrict__ y, QAct q) {
+    int64_t t = blockIdx.x;
+    int64_t src = row_idx ? row_idx[t] : t;
+    const float *xr = x + src * (int64_t)K;
+    __shared__ float partial[16];
+    __shared__ float s_scale;
+    int tid = threadIdx.x;
+    int vec_end = K >= 16 ? (K / 16) * 16 : 0;
+    if (tid < 16) {
+        float acc = 0.0f;
+        for (int i = tid; i < vec_end; i += 16) acc = __fadd_rn(acc, __fmul_rn(xr[i], xr[i]));
+        partial[tid] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double sum = 0.0;
+        if (vec_end > 0) sum = __dadd_rn((double)vsum8(partial), (double)vsum8(partial + 8));
+        for (int i = vec_end; i < K; i++) sum = __dadd_rn(sum, __dmul_rn((double)xr[i], (double)xr[i]));
+        float ms = __double2float_rn(__ddiv_rn(sum, (double)K));
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    }
+    __syncthreads();
+    float scale = s_scale;
+    int lane = tid & 31, wid = tid >> 5;
+    int nb = K / 32;
+    for (int b = wid; b < nb; b += blockDim.x / 32) {
+        int i = b * 32 + lane;
+        float v = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+        if (y) y[t * K + i] = v;
+        float d;
+        int sum;
+        int qv = quantize_lane(v, d, sum);
+        int64_t o = t * K + i;
+        if (q.a8) q.a8[o] = (int8_t)qv;
+        if (q.a16) q.a16[o] = __int2half_rn(qv);
+        if (lane == 0) {
+            int64_t so = t * nb + b;
+            q.da[so] = d;
+            if (q.ds) q.ds[so] = __fmul_rn(d, (float)sum);
+            if (q.sums) q.sums[so] = sum;
+        }
+    }
+}
+
+cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
+                                 float eps, float *y, const QAct &q, cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    k_rmsnorm_quant<<<(unsigned)M, 128, 0, s>>>(x, row_idx, K, w, eps, y, q);
+    return cudaGetLastError();
+}
+
+// QuantMatMul.GatherRows + Dequantizer legacy decode (QuantMatMul.cs:534-545,
+// Dequantizer.cs:127-213): one warp per (token, block), lane j -> element j.
+template <int TYPE>
+__global__ void k_embed(const uint8_t *__restrict__ table, int64_t rows, int64_t row_bytes, int64_t K,
+                        const int32_t *__restrict__ ids, int64_t M, float *__restrict__ h, int32_t *err) {
+    int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    int64_t nb = K / 32;
+    if (warp >= M * nb) return;
+    int64_t t = warp / nb, b = warp % nb;
+    int id = ids[t];
+    if (id < 0 || id >= rows) {
+        if (lane == 0 && b == 0) atomicExch(err, 2);
+        h[t * K + b * 32 + lane] = 0.0f;
+        return;
+    }
+    const uint8_t *row = table + (int64_t)id * row_bytes;
+    float v;
+    if (TYPE == T_F32) {
+        v = reinterpret_cast<const float *>(row)[b * 32 + lane];
+    } else if (TYPE == T_F16) {
+        v = h2f(ld_u16(row + (b * 32 + lane) * 2));
+    } else {
+        const uint8_t *blk = row + b * block_bytes(TYPE);
+        float d = h2f(ld_u16(blk));
+        int wv = weight_at<TYPE>(blk, lane);
+        if (has_offset(TYPE))
+            v = __fadd_rn(__fmul_rn(d, (float)wv), h2f(ld_u16(blk + 2)));
+        else
+            v = __fmul_rn(d, (float)wv);
+    }
+    h[t * K + b * 32 + lane] = v;
+}
+
+cudaError_t launch_embed(const DevWeight &emb, const int32_t *ids, int64_t M, float *h, int32_t *err,
+                         cudaStream_t s) {
+    int64_t warps = M * (emb.cols / 32);
+    if (warps == 0) return cudaSuccess;
+    int threads = 256;
+    unsigned blocks = (unsigned)((warps * 32 + threads - 1) / threads);
+#define EMB(T) k_embed<T><<<blocks, threads, 0, s>>>(emb.data, emb.rows, emb.row_bytes, emb.cols, ids, M, h, err)
+    switch (emb.type) {
+    case T_F32: EMB(T_F32); break;
+    case T_F16: EMB(T_F16); break;
+    case T_Q4_0: EMB(T_Q4_0); break;
+    case T_Q4_1: EMB(T_Q4_1); break;
+    case T_Q5_0: EMB(T_Q5_0); break;
+    case T_Q5_1: EMB(T_Q5_1); break;
+    case T_Q8_0: EMB(T_Q8_0); break;
+    default: return cudaErrorInvalidValue;
+    }
+#undef EMB
+    return cudaGetLastError();
+}
+
+// Scale (and offset) planes [K/32][rows] in f32, read once at upload.
+__global__ void k_build_planes(const uint8_t *__restrict__ data, int64_t rows, int64_t row_bytes, int64_t nb,
+                               int bb, int with_offset, float *__restrict__ scale, float *__restrict__ offset) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nb) return;
+    int64_t b = i / rows, r = i % rows;
+    const uint8_t *blk = data + r * row_bytes + b * bb;
+    scale[i] = h2f(ld_u16(blk));
+    if (with_offset) offset[i] = h2f(ld_u16(blk + 2));
+}
+
+cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s) {
+    int bb = block_bytes(w.type);
+    if (!bb || !w.scale_plane) return cudaSuccess;
+    int64_t n = w.rows * (w.cols / 32);
+    k_build_planes<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, bb,
+                                                                has_offset(w.type) ? 1 : 0, w.scale_plane,
+                                                                w.offset_plane);
+    return cudaGetLastError();
+}
+
+}  // namespace shield

@@ -1,0 +1,121 @@
+"""GPU parity of the quantized GEMM through the C ABI against the oracle:
+per-block int32 dots bit-exact, outputs bit-identical, the reference's tiling
+and row-subset invariants (MatMulTilingTests.cs), and error behaviour."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from llm_shield_b200 import binding, synth
+from helpers import random_weights
+
+pytestmark = pytest.mark.gpu
+INT_TYPES = [synth.Q8_0, synth.Q4_0, synth.Q4_1, synth.Q5_0, synth.Q5_1]
+SWEEP_SHAPES = [(3072, 3072), (1024, 3072), (9216, 3072), (3072, 9216), (4096, 3072), (3072, 4096)]
+
+
+@pytest.fixture(scope="module")
+def ctx(shield_lib):
+    c = binding.ShieldContext(1)
+    c.set_config(synth.small_spec())
+    yield c
+    c.close()
+
+
+def upload(ctx, name, qtype, rows, cols, w):
+    ctx.upload(name, qtype, rows, cols, w)
+
+
+@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("qtype", INT_TYPES)
+def test_block_dots_bit_exact(ctx, qtype, path):
+    """Per-block int32 dot products equal the oracle's i = -z·Σa + Σ u·a."""
+    rows, cols, tokens = 256, 512, 19
+    w = random_weights(qtype, rows, cols, seed=qtype)
+    x = np.random.default_rng(qtype).standard_normal((tokens, cols)).astype(np.float32) * 3
+    upload(ctx, "blk.0.attn_q.weight", qtype, rows, cols, w)
+    expect = oracle.block_dots(qtype, w, rows, cols, x, tokens)
+    try:
+        got = ctx.block_dots("blk.0.attn_q.weight", x, tokens, rows, cols, path=path)
+    except binding.ShieldError as e:
+        if path == 2 and e.code == binding.ERR_UNSUPPORTED:
+            pytest.skip("tensor-core path not built for this shape")
+        raise
+    np.testing.assert_array_equal(got, expect)
+
+
+@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("qtype", INT_TYPES)
+@pytest.mark.parametrize("rows,cols,tokens", [(100, 256, 13), (256, 768, 130), (128, 3072, 64)])
+def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
+    w = random_weights(qtype, rows, cols, seed=rows + cols + qtype)
+    x = np.random.default_rng(tokens).uniform(-1, 1, (tokens, cols)).astype(np.float32)
+    upload(ctx, "blk.0.attn_k.weight", qtype, rows, cols, w)
+    expect = oracle.qmatmul(qtype, w, rows, cols, x, tokens)
+    ctx.set_gemm_path(path)
+    try:
+        got = ctx.qmatmul("blk.0.attn_k.weight", x, tokens, rows)
+    except binding.ShieldError as e:
+        if path == 2 and e.code == binding.ERR_UNSUPPORTED:
+            pytest.skip("tensor-core path does not take this shape")
+        raise
+    finally:
+        ctx.set_gemm_path(0)
+    np.testing.assert_array_equal(got, expect)
+
+
+@pytest.mark.parametrize("qtype", [synth.Q4_0, synth.Q5_0, synth.Q5_1, synth.Q8_0])
+@pytest.mark.parametrize("rows,cols", SWEEP_SHAPES)
+def test_sweep_shapes_match_oracle(ctx, qtype, rows, cols):
+    """The isolated-GEMM sweep's shapes on the synthetic N(0, 0.02) weights at
+    M = 64 (plus a single token), bit-identical to the oracle."""
+    w = synth.tensor(qtype, rows, cols, seed=77, stream=rows * 7 + cols)
+    upload(ctx, "blk.0.ffn_gate.weight", qtype, rows, cols, w)
+    for M in (1, 64):
+        x = np.random.default_rng(M).standard_normal((M, cols)).astype(np.float32)
+        np.testing.assert_array_equal(ctx.qmatmul("blk.0.ffn_gate.weight", x, M, rows),
+                                      oracle.qmatmul(qtype, w, rows, cols, x, M))
+
+
+@pytest.mark.parametrize("qtype", INT_TYPES)
+def test_token_result_does_not_depend_on_batch(ctx, qtype):
+    """MatMulTilingTests.cs:42-65 through the C ABI (and across kernels)."""
+    rows, cols, tokens = 100, 256, 13
+    w = random_weights(qtype, rows, cols, seed=3)
+    x = np.random.default_rng(4).uniform(-1, 1, (tokens, cols)).astype(np.float32)
+    upload(ctx, "blk.0.attn_v.weight", qtype, rows, cols, w)
+    together = ctx.qmatmul("blk.0.attn_v.weight", x, tokens, rows)
+    for t in range(tokens):
+        np.testing.assert_array_equal(ctx.qmatmul("blk.0.attn_v.weight", x[t:t + 1], 1, rows)[0], together[t])
+    np.testing.assert_array_equal(ctx.qmatmul("blk.0.attn_v.weight", x[5:], 8, rows), together[5:])
+
+
+@pytest.mark.parametrize("qtype", INT_TYPES)
+def test_row_subset_bit_identical(ctx, qtype):
+    """MatMulTilingTests.cs:67-95: out of order, repeated, across group boundaries."""
+    rows, cols, tokens = 100, 256, 5
+    ids = [99, 0, 57, 57, 8, 7, 64, 63, 98]
+    w = random_weights(qtype, rows, cols, seed=5)
+    x = np.random.default_rng(6).uniform(-1, 1, (tokens, cols)).astype(np.float32)
+    upload(ctx, "blk.0.attn_output.weight", qtype, rows, cols, w)
+    full = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows)
+    sub = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows, row_ids=ids)
+    np.testing.assert_array_equal(sub, full[:, ids])
+
+
+def test_row_subset_rejects_ids_outside_the_matrix(ctx):
+    rows, cols = 100, 256
+    upload(ctx, "blk.0.ffn_up.weight", synth.Q4_0, rows, cols, random_weights(synth.Q4_0, rows, cols, 1))
+    x = np.zeros((1, cols), np.float32)
+    with pytest.raises(binding.ShieldArgumentOutOfRange):
+        ctx.qmatmul("blk.0.ffn_up.weight", x, 1, rows, row_ids=[0, rows])
+
+
+def test_unsupported_type_and_bad_sizes_are_rejected(ctx):
+    with pytest.raises(binding.ShieldError) as e:
+        ctx.upload("blk.0.ffn_down.weight", 10, 64, 64, np.zeros(64 * 64, np.uint8))  # Q2_K
+    assert e.value.code == binding.ERR_UNSUPPORTED
+    with pytest.raises(binding.ShieldError) as e:
+        ctx.upload("blk.0.ffn_down.weight", synth.Q4_0, 64, 64, np.zeros(10, np.uint8))
+    assert e.value.code == binding.ERR_ARG
