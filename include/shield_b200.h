@@ -172,6 +172,27 @@ enum {
 shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int32_t *ids, int32_t n,
                                       int32_t layer, int32_t what, float *out);
 
+/* Device-side accounting of the context's work, for benchmarks. */
+typedef struct shield_timing {
+    double forward_ms;      /* device time of forward passes, from the first kernel of a
+                               micro-batch (its ids already on the GPU) to its verdict logits */
+    double gemm_ms;         /* device time inside quantized-GEMM launches (level 2 only) */
+    double gemm_ops;        /* their algorithmic ops, 2*M*N*K */
+    double gemm_bytes;      /* their algorithmic bytes: packed weights + int8 activations and
+                               scales + f32 outputs */
+    int64_t gemm_launches;  /* quantized-GEMM launches */
+    int64_t kernel_launches;/* every kernel the library launched */
+    int64_t tokens;         /* tokens forwarded */
+    int64_t requests;       /* requests scored */
+    int64_t h2d_bytes;      /* host->device bytes of scoring calls */
+    int64_t d2h_bytes;      /* device->host bytes of scoring calls */
+} shield_timing;
+
+/* level 0: off; 1: forward intervals and counters; 2: also every GEMM launch. */
+shield_status shield_set_timing(shield_ctx *ctx, int32_t level);
+/* Reads (after synchronizing) and optionally resets the accounting of one GPU. */
+shield_status shield_read_timing(shield_ctx *ctx, int32_t device, shield_timing *out, int32_t reset);
+
 /* The CUDA stream (cudaStream_t) the context enqueues work for `device` on. */
 shield_status shield_device_stream(shield_ctx *ctx, int32_t device, void **stream);
 

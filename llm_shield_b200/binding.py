@@ -45,10 +45,18 @@ class ShieldConfig(C.Structure):
     ]
 
 
+class ShieldTiming(C.Structure):
+    _fields_ = [("forward_ms", C.c_double), ("gemm_ms", C.c_double), ("gemm_ops", C.c_double),
+                ("gemm_bytes", C.c_double), ("gemm_launches", C.c_int64), ("kernel_launches", C.c_int64),
+                ("tokens", C.c_int64), ("requests", C.c_int64), ("h2d_bytes", C.c_int64),
+                ("d2h_bytes", C.c_int64)]
+
+
 EXPORTS = [
     "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
     "shield_score_batch", "shield_qmatmul", "shield_qmatmul_device", "shield_debug_block_dots",
-    "shield_set_gemm_path", "shield_debug_activation", "shield_device_stream", "shield_last_error",
+    "shield_set_gemm_path", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
+    "shield_device_stream", "shield_last_error",
 ]
 
 _lib = None
@@ -76,6 +84,8 @@ def lib() -> C.CDLL:
         L.shield_set_gemm_path.argtypes = [P, C.c_int32]
         L.shield_debug_activation.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_int32, P]
         L.shield_device_stream.argtypes = [P, C.c_int32, C.POINTER(P)]
+        L.shield_set_timing.argtypes = [P, C.c_int32]
+        L.shield_read_timing.argtypes = [P, C.c_int32, C.POINTER(ShieldTiming), C.c_int32]
         L.shield_last_error.restype = C.c_char_p
         for name in EXPORTS:
             f = getattr(L, name)
@@ -207,6 +217,14 @@ class ShieldContext:
         out = np.zeros((ids.size, width), np.float32)
         _check(lib().shield_debug_activation(self._h, device, _p(ids), ids.size, layer, what, _p(out)))
         return out
+
+    def set_timing(self, level: int):
+        _check(lib().shield_set_timing(self._h, level))
+
+    def read_timing(self, device: int = 0, reset: bool = True) -> dict:
+        t = ShieldTiming()
+        _check(lib().shield_read_timing(self._h, device, C.byref(t), int(reset)))
+        return {name: getattr(t, name) for name, _ in ShieldTiming._fields_}
 
     def stream(self, device: int = 0) -> int:
         s = C.c_void_p()

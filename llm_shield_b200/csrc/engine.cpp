@@ -169,9 +169,44 @@ struct Scratch {  // grow-on-demand buffers of the single-GEMM entry points
     }
 };
 
+// Device-side accounting (shield_set_timing / shield_read_timing).
+struct Timing {
+    int level = 0;
+    std::vector<cudaEvent_t> pool;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> fwd, gemm;
+    double gemm_ops = 0, gemm_bytes = 0;
+    int64_t gemm_launches = 0, launches = 0, tokens = 0, requests = 0, h2d = 0, d2h = 0;
+    cudaEvent_t event() {
+        if (pool.empty()) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            return e;
+        }
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    void recycle() {
+        for (auto &p : fwd) { pool.push_back(p.first); pool.push_back(p.second); }
+        for (auto &p : gemm) { pool.push_back(p.first); pool.push_back(p.second); }
+        fwd.clear();
+        gemm.clear();
+    }
+    void reset() {
+        recycle();
+        gemm_ops = gemm_bytes = 0;
+        gemm_launches = launches = tokens = requests = h2d = d2h = 0;
+    }
+    ~Timing() {
+        recycle();
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+
 struct Device {
     int ordinal = 0;
     cudaStream_t stream = nullptr;
+    Timing timing;
     std::unordered_map<std::string, Tensor> tensors;
     float *cos_t = nullptr, *sin_t = nullptr, *temp = nullptr;
     Buffers buf;
@@ -210,14 +245,40 @@ static void check_launch(cudaError_t e, const char *what) {
     if (e != cudaSuccess) throw Error(SHIELD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Counts one launch (and, at timing level 2, brackets GEMM launches with events).
+static void count_launch(Device &d) { d.timing.launches++; }
+
 static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, int64_t ldy, int epi) {
+    Timing &T = d.timing;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (T.level >= 2) {
+        e0 = T.event();
+        e1 = T.event();
+        if (e0) cudaEventRecord(e0, d.stream);
+    }
+    bool done = false;
     if (C.gemm_path != 1 && gemm_tc_supports(W.w, q.M)) {
         cudaError_t e = launch_gemm_tc(W.w, q, y, ldy, epi, d.buf.err ? d.buf.err : nullptr, d.stream);
-        if (e == cudaSuccess) return;
-        if (e != cudaErrorNotSupported) check_launch(e, "tensor-core GEMM");
+        if (e == cudaSuccess)
+            done = true;
+        else if (e != cudaErrorNotSupported)
+            check_launch(e, "tensor-core GEMM");
     }
-    if (C.gemm_path == 2) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
-    check_launch(launch_gemm_simt(W.w, nullptr, W.w.rows, q, y, ldy, epi, d.stream), "CUDA-core GEMM");
+    if (!done) {
+        if (C.gemm_path == 2) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
+        check_launch(launch_gemm_simt(W.w, nullptr, W.w.rows, q, y, ldy, epi, d.stream), "CUDA-core GEMM");
+    }
+    count_launch(d);
+    if (T.level >= 1) {
+        T.gemm_launches++;
+        T.gemm_ops += 2.0 * (double)q.M * (double)W.w.rows * (double)W.w.cols;
+        T.gemm_bytes += (double)W.w.rows * (double)W.w.row_bytes + (double)q.M * (double)W.w.cols * 1.125 +
+                        (double)q.M * (double)W.w.rows * (epi == EPI_ADD ? 8.0 : 4.0);
+    }
+    if (e1 && e0) {
+        cudaEventRecord(e1, d.stream);
+        T.gemm.emplace_back(e0, e1);
+    }
 }
 
 static QAct qact(Buffers &b, int64_t M, int64_t K) {
@@ -300,11 +361,21 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         h_last[r] = (int32_t)(st + B.len[r] - 1);
     }
     SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
+    Timing &T = d.timing;
+    cudaEvent_t f0 = nullptr, f1 = nullptr;
+    if (T.level >= 1) {
+        T.h2d += (3 * M + R) * 4;
+        T.tokens += M;
+        T.requests += R;
+        f0 = T.event();
+        f1 = T.event();
+        if (f0) cudaEventRecord(f0, s);
+    }
     const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_start = b.meta + 2 * M, *d_last = b.meta + 3 * M;
     int max_len = *std::max_element(B.len.begin(), B.len.end());
 
     const Tensor &emb = d.get("token_embd.weight");
-    check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
+    count_launch(d), check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
     const float scale = 1.0f / sqrtf((float)c.head_dim);
     auto cap = [&](int l, int what, const float *src, int64_t width) {
         if (l == capture_layer && capture && capture_what == what)
@@ -324,33 +395,33 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
 
         QAct qa = qact(b, M, c.hidden);
         bool want_norm = l == capture_layer && capture_what == SHIELD_ACT_ATTN_NORM;
-        check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, an.vec, c.eps, want_norm ? b.ctx : nullptr, qa, s),
+        count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, an.vec, c.eps, want_norm ? b.ctx : nullptr, qa, s),
                      "attn norm");
         cap(l, SHIELD_ACT_ATTN_NORM, b.ctx, c.hidden);
         gemm(C, d, wq, qa, b.q, c.qdim(), EPI_STORE);
         gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
         gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
-        check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
+        count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
                                  d.temp, s), "rope q");
-        check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
+        count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
                                  nullptr, s), "rope k");
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());
-        check_launch(launch_attention(b.q, b.k, b.v, b.ctx, d_start, M, c.n_heads, c.n_kv_heads, c.head_dim, scale,
+        count_launch(d), check_launch(launch_attention(b.q, b.k, b.v, b.ctx, d_start, M, c.n_heads, c.n_kv_heads, c.head_dim, scale,
                                       max_len, s), "attention");
         cap(l, SHIELD_ACT_ATTN_WEIGHTED, b.ctx, c.qdim());
         QAct qc = qact(b, M, c.qdim());
-        check_launch(launch_quantize(b.ctx, M, c.qdim(), c.qdim(), qc, s), "quantize context");
+        count_launch(d), check_launch(launch_quantize(b.ctx, M, c.qdim(), c.qdim(), qc, s), "quantize context");
         gemm(C, d, wo, qc, b.h, c.hidden, EPI_ADD);
         cap(l, SHIELD_ACT_POST_ATTN, b.h, c.hidden);
 
-        check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, fn.vec, c.eps, nullptr, qa, s), "ffn norm");
+        count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, fn.vec, c.eps, nullptr, qa, s), "ffn norm");
         gemm(C, d, wg, qa, b.g, c.ffn, EPI_STORE);
         gemm(C, d, wu, qa, b.u, c.ffn, EPI_STORE);
-        check_launch(launch_swiglu(b.g, b.u, M * c.ffn, s), "swiglu");
+        count_launch(d), check_launch(launch_swiglu(b.g, b.u, M * c.ffn, s), "swiglu");
         QAct qf = qact(b, M, c.ffn);
-        check_launch(launch_quantize(b.g, M, c.ffn, c.ffn, qf, s), "quantize ffn");
+        count_launch(d), check_launch(launch_quantize(b.g, M, c.ffn, c.ffn, qf, s), "quantize ffn");
         gemm(C, d, wd, qf, b.h, c.hidden, EPI_ADD);
         cap(l, SHIELD_ACT_OUTPUT, b.h, c.hidden);
     }
@@ -358,9 +429,19 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         // last position of every request -> final norm -> verdict rows of the tied head
         const Tensor &on = d.get("output_norm.weight");
         QAct qh = qact(b, R, c.hidden);
-        check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
-        check_launch(launch_gemm_simt(emb.w, b.verdict, nv, qh, b.logits, nv, EPI_STORE, s), "verdict head");
+        count_launch(d), check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
+        count_launch(d), check_launch(launch_gemm_simt(emb.w, b.verdict, nv, qh, b.logits, nv, EPI_STORE, s), "verdict head");
+        if (f1 && f0) {
+            cudaEventRecord(f1, s);
+            T.fwd.emplace_back(f0, f1);
+            f0 = f1 = nullptr;
+        }
         SHIELD_CUDA(cudaMemcpyAsync(b.h_logits, b.logits, (size_t)R * nv * 4, cudaMemcpyDeviceToHost, s));
+        if (T.level >= 1) T.d2h += (int64_t)R * nv * 4;
+    }
+    if (f1 && f0) {
+        cudaEventRecord(f1, s);
+        T.fwd.emplace_back(f0, f1);
     }
     check_device_error(d);
 }
@@ -867,6 +948,44 @@ shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int
         B.len = {n};
         B.tokens = n;
         forward_batch(C, d, ids, B, 0, nullptr, layer, what, out);
+    });
+}
+
+shield_status shield_set_timing(shield_ctx *ctx, int32_t level) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        if (level < 0 || level > 2) throw Error(SHIELD_ERR_ARG, "level must be 0, 1 or 2");
+        for (auto &d : ctx->c.devs) d->timing.level = level;
+    });
+}
+
+shield_status shield_read_timing(shield_ctx *ctx, int32_t device, shield_timing *out, int32_t reset) {
+    return guarded([&] {
+        if (!ctx || !out) throw Error(SHIELD_ERR_ARG, "null argument");
+        Device &d = device_of(ctx->c, device);
+        SHIELD_CUDA(cudaStreamSynchronize(d.stream));
+        Timing &T = d.timing;
+        shield_timing t{};
+        for (auto &p : T.fwd) {
+            float ms = 0;
+            SHIELD_CUDA(cudaEventElapsedTime(&ms, p.first, p.second));
+            t.forward_ms += ms;
+        }
+        for (auto &p : T.gemm) {
+            float ms = 0;
+            SHIELD_CUDA(cudaEventElapsedTime(&ms, p.first, p.second));
+            t.gemm_ms += ms;
+        }
+        t.gemm_ops = T.gemm_ops;
+        t.gemm_bytes = T.gemm_bytes;
+        t.gemm_launches = T.gemm_launches;
+        t.kernel_launches = T.launches;
+        t.tokens = T.tokens;
+        t.requests = T.requests;
+        t.h2d_bytes = T.h2d;
+        t.d2h_bytes = T.d2h;
+        *out = t;
+        if (reset) T.reset();
     });
 }
 

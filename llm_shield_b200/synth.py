@@ -54,6 +54,9 @@ def lib() -> C.CDLL:
 
 
 def threads() -> int:
+    env = os.environ.get("SHIELD_SYNTH_THREADS")
+    if env:
+        return max(1, int(env))
     return max(1, len(os.sched_getaffinity(0)))
 
 
