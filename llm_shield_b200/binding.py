@@ -136,9 +136,10 @@ class ShieldContext:
         _check(lib().shield_open(device_mask, C.byref(self._h)))
 
     def close(self):
-        if self._h:
-            lib().shield_close(self._h)
-            self._h = C.c_void_p()
+        h = getattr(self, "_h", None)
+        if h and _lib is not None:
+            _lib.shield_close(h)
+        self._h = C.c_void_p()
 
     def __del__(self):
         self.close()

@@ -1,18 +1,546 @@
-// tcgen05 tensor-core GEMM (placeholder until the kernel lands).
+// tcgen05 tensor-core GEMM for GGUF legacy-quantized weights (sm_100a).
+//
+// y[t, n] = Σ_b fma-chain( float(i_b[t, n]) · (d_w[n, b] · d_a[t, b]) )     (+ Q4_1/Q5_1 offsets)
+// with i_b the exact int32 dot of block b (IntegerGemm.cs:371-457): the same
+// per-output operation sequence as the reference and the oracle, so outputs
+// are bit-identical to theirs.
+//
+// Tile: 128 tokens (TMEM lanes / UMMA M) x 128 output features (UMMA N).
+// Per 32-element quant block the tile needs its own int32 result, because the
+// f32 chain scales every block separately; one block is one UMMA K-step.
+//
+//   warp 0      TMA producer: activation tiles (f16 holding the int8 values,
+//               128B-swizzled K-major) and raw GGUF weight chunks (8 blocks per
+//               row, bytes unchanged)
+//   warp 1      TMEM owner + MMA issuer: two tcgen05.mma.kind::f16 (K=16) per
+//               block into one of four 128-column TMEM slots
+//   warps 2-3   unpack raw blocks in registers (nibbles, 5th bits, Q8 bytes) to
+//               f16 integers in the canonical SW128 K-major layout; widen the
+//               f16 block scales (and offsets) to f32
+//   warps 4-11  epilogue: tcgen05.ld the slot, apply the block's f32 scaling
+//               chain per output, write (or add to) y
+//
+// kind::f16 rather than kind::i8: products of 8-bit integers summed over one
+// block stay below 2^20, so the f32 accumulator holds the exact int32 sum and
+// the epilogue needs no integer->float conversion (the epilogue's f32 pipe,
+// not the tensor pipe, bounds this kernel).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "ops.h"
 
 namespace shield {
+namespace tc {
 
-bool gemm_tc_supports(const DevWeight &w, int64_t M) { return false; }
+constexpr int BM = 128;          // tokens per tile (TMEM lanes)
+constexpr int BN = 128;          // output features per tile (TMEM columns per slot)
+constexpr int STAGES = 3;        // activation / unpacked-weight stages, 2 blocks each
+constexpr int RAW_STAGES = 2;    // raw weight chunks in flight
+constexpr int SC_STAGES = 2;     // f32 scale chunks in flight
+constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns)
+constexpr int CHUNK = 8;         // blocks per raw chunk (TMA inner box = 8 blocks)
+constexpr int THREADS = 384;
+constexpr int EPI_WARPS = 8;
+constexpr int UNPACK_THREADS = 64;
+
+__host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int TYPE>
+struct Smem {
+    static constexpr int BB = block_bytes(TYPE);
+    static constexpr int RAW_ROW = CHUNK * BB;   // bytes of one row's chunk
+    static constexpr int RAW_BYTES = BN * RAW_ROW;
+    static constexpr int A_BYTES = BM * 128;     // 64 f16 per row
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int SC_FLOATS = CHUNK * BN * (has_offset(TYPE) ? 2 : 1);
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+    static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
+    static constexpr int OFF_SC = OFF_RAW + RAW_STAGES * align_up(RAW_BYTES, 1024);
+    static constexpr int OFF_BAR = OFF_SC + SC_STAGES * SC_FLOATS * 4;
+    // barriers: a_full, a_empty, b_full, b_empty (STAGES each), raw_full, raw_empty,
+    // sc_full, sc_empty, t_full, t_empty
+    static constexpr int NBAR = 4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + 2 * NSLOT;
+    static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+};
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~2 s of SM clock, raising the CTA's abort flag
+// and the kernel's error word, so a lost arrival can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int32_t *err) {
+    if (mbar_try(bar, parity)) return true;
+    long long t0 = clock64();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 255) == 255) {
+            if (*abort_flag) return false;
+            if (clock64() - t0 > 4000000000LL) {
+                *abort_flag = 1;
+                if (err) atomicExch(err, 3);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128B-swizzled operand: 8-row groups 1024 B apart (SBO), LBO unused (1),
+// descriptor version 1 (sm_100), layout SWIZZLE_128B (2).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M=128, N=BN.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------ unpacking
+
+// Four payload bytes (one per lane of a 32-bit word, each < 256) -> two f16x2
+// words holding (byte - z) exactly: 0x6400|b is the f16 1024+b, minus 1024+z.
+__device__ __forceinline__ void bytes_to_f16(uint32_t w, __half2 bias, uint32_t &lo, uint32_t &hi) {
+    uint32_t a = __byte_perm(w, 0x64646464u, 0x4140);
+    uint32_t b = __byte_perm(w, 0x64646464u, 0x4342);
+    __half2 ha = __hsub2(*reinterpret_cast<__half2 *>(&a), bias);
+    __half2 hb = __hsub2(*reinterpret_cast<__half2 *>(&b), bias);
+    lo = *reinterpret_cast<uint32_t *>(&ha);
+    hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+
+// bit i of the 4-bit x -> bit 4 of byte i (the Q5 fifth bits as 0x10 per byte)
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return ((x * 0x00204081u) & 0x01010101u) << 4; }
+
+__device__ __forceinline__ uint32_t ld_smem_u32_2aligned(const uint8_t *p) {
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
+    return (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+}
+
+// One raw block -> 32 f16 integers (w = u - z) as 16 words, in weight order.
+template <int TYPE>
+__device__ __forceinline__ void unpack_block(const uint8_t *blk, uint32_t (&o)[16]) {
+    constexpr int Z = zero_point(TYPE);
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)(0x6400 + Z)));
+    if (TYPE == T_Q8_0) {
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            uint32_t v = ld_smem_u32_2aligned(blk + 2 + 4 * w) ^ 0x80808080u;  // u = q + 128
+            bytes_to_f16(v, bias, o[2 * w], o[2 * w + 1]);
+        }
+    } else {
+        const uint8_t *qs = blk + qs_offset(TYPE);
+        uint32_t qh = 0;
+        if (TYPE == T_Q5_0 || TYPE == T_Q5_1) qh = ld_smem_u32_2aligned(blk + qh_offset(TYPE));
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            uint32_t q = ld_smem_u32_2aligned(qs + 4 * w);
+            uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
+            if (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
+                lo |= spread4((qh >> (4 * w)) & 0xFu);
+                hi |= spread4((qh >> (16 + 4 * w)) & 0xFu);
+            }
+            // elements 4w..4w+3 (low nibbles) and 16+4w..16+4w+3 (high nibbles)
+            bytes_to_f16(lo, bias, o[2 * w], o[2 * w + 1]);
+            bytes_to_f16(hi, bias, o[8 + 2 * w], o[8 + 2 * w + 1]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <int TYPE, int EPI, bool DOTS>
+__global__ void __launch_bounds__(THREADS, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+          const float *__restrict__ da, const float *__restrict__ ds, float *__restrict__ y, int64_t ldy, int M, int N,
+          int nb, int32_t *__restrict__ err, int32_t *__restrict__ dots) {
+    using L = Smem<TYPE>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+
+    uint32_t bar = sbase + L::OFF_BAR;
+    auto a_full = [&](int s) { return bar + 8 * s; };
+    auto a_empty = [&](int s) { return bar + 8 * (STAGES + s); };
+    auto b_full = [&](int s) { return bar + 8 * (2 * STAGES + s); };
+    auto b_empty = [&](int s) { return bar + 8 * (3 * STAGES + s); };
+    auto raw_full = [&](int s) { return bar + 8 * (4 * STAGES + s); };
+    auto raw_empty = [&](int s) { return bar + 8 * (4 * STAGES + RAW_STAGES + s); };
+    auto sc_full = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + s); };
+    auto sc_empty = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + SC_STAGES + s); };
+    auto t_full = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + s); };
+    auto t_empty = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + NSLOT + s); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::OFF_MISC + 4);
+    float *sc_base = reinterpret_cast<float *>(smem + L::OFF_SC);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(a_full(s), 1);
+            mbar_init(a_empty(s), 1);
+            mbar_init(b_full(s), UNPACK_THREADS);
+            mbar_init(b_empty(s), 1);
+        }
+        for (int s = 0; s < RAW_STAGES; s++) {
+            mbar_init(raw_full(s), 1);
+            mbar_init(raw_empty(s), UNPACK_THREADS);
+        }
+        for (int s = 0; s < SC_STAGES; s++) {
+            mbar_init(sc_full(s), UNPACK_THREADS);
+            mbar_init(sc_empty(s), EPI_WARPS);
+        }
+        for (int s = 0; s < NSLOT; s++) {
+            mbar_init(t_full(s), 1);
+            mbar_init(t_empty(s), EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(NSLOT * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int npairs = nb / 2, nchunks = nb / CHUNK;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            for (int p = 0; p < npairs; p++) {
+                if ((2 * p) % CHUNK == 0) {
+                    int c = (2 * p) / CHUNK, rs = c % RAW_STAGES;
+                    if (!mbar_wait(raw_empty(rs), ((c / RAW_STAGES) & 1) ^ 1, abort_flag, err)) break;
+                    mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
+                    tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w, c * (L::RAW_ROW / 2),
+                                n0, raw_full(rs));
+                }
+                int s = p % STAGES;
+                if (!mbar_wait(a_empty(s), ((p / STAGES) & 1) ^ 1, abort_flag, err)) break;
+                mbar_expect_tx(a_full(s), L::A_BYTES);
+                tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &map_a, 2 * p * 32, m0, a_full(s));
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            for (int p = 0; p < npairs; p++) {
+                int s = p % STAGES;
+                uint32_t ph = (p / STAGES) & 1;
+                if (!mbar_wait(a_full(s), ph, abort_flag, err)) break;
+                if (!mbar_wait(b_full(s), ph, abort_flag, err)) break;
+                tc_fence_after();
+                bool ok = true;
+                for (int jb = 0; jb < 2; jb++) {
+                    int kb = 2 * p + jb, slot = kb % NSLOT;
+                    if (!mbar_wait(t_empty(slot), ((kb / NSLOT) & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t a_addr = sbase + L::OFF_A + s * L::A_BYTES + jb * 64;
+                    uint32_t b_addr = sbase + L::OFF_B + s * L::B_BYTES + jb * 64;
+#pragma unroll
+                    for (int k = 0; k < 2; k++)
+                        umma_f16(tmem_base + slot * BN, umma_desc_sw128(a_addr + 32 * k),
+                                 umma_desc_sw128(b_addr + 32 * k), k);
+                    umma_commit(t_full(slot));
+                }
+                if (!ok) break;
+                umma_commit(a_empty(s));
+                umma_commit(b_empty(s));
+            }
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------ unpackers
+        const int ut = threadIdx.x - 64;
+        for (int c = 0; c < nchunks; c++) {
+            int rs = c % RAW_STAGES, ss = c % SC_STAGES;
+            if (!mbar_wait(raw_full(rs), (c / RAW_STAGES) & 1, abort_flag, err)) break;
+            if (!mbar_wait(sc_empty(ss), ((c / SC_STAGES) & 1) ^ 1, abort_flag, err)) break;
+            const uint8_t *raw = smem + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024);
+            float *sc = sc_base + ss * L::SC_FLOATS;
+            bool ok = true;
+            for (int q = 0; q < CHUNK / 2; q++) {
+                int p = c * (CHUNK / 2) + q, s = p % STAGES;
+                if (!mbar_wait(b_empty(s), ((p / STAGES) & 1) ^ 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *bst = smem + L::OFF_B + s * L::B_BYTES;
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int r = ut + rr * 64;
+#pragma unroll
+                    for (int jb = 0; jb < 2; jb++) {
+                        const int j = 2 * q + jb;
+                        const uint8_t *blk = raw + r * L::RAW_ROW + j * L::BB;
+                        uint32_t o[16];
+                        unpack_block<TYPE>(blk, o);
+#pragma unroll
+                        for (int cc = 0; cc < 4; cc++) {
+                            int chunk16 = jb * 4 + cc;
+                            uint4 v = make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
+                            *reinterpret_cast<uint4 *>(bst + r * 128 + ((chunk16 ^ (r & 7)) << 4)) = v;
+                        }
+                        sc[j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk));
+                        if (has_offset(TYPE)) sc[CHUNK * BN + j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                    }
+                }
+                fence_proxy_async();
+                mbar_arrive(b_full(s));
+            }
+            if (!ok) break;
+            mbar_arrive(raw_empty(rs));
+            mbar_arrive(sc_full(ss));
+        }
+    } else {
+        // ------------------------------------------------------ epilogue
+        const int q = warp & 3;              // TMEM lane quarter this warp may access
+        const int g = (warp - 4) >> 2;       // column half (0: 0..63, 1: 64..127)
+        const int t = q * 32 + lane;         // token within the tile
+        const int m = m0 + t;
+        const bool row_ok = m < M;
+        const bool warp_live = m0 + q * 32 < M;
+        float f[64];
+#pragma unroll
+        for (int i = 0; i < 64; i++) f[i] = 0.0f;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * 64;
+        for (int c = 0; c < nchunks; c++) {
+            int ss = c % SC_STAGES;
+            if (!mbar_wait(sc_full(ss), (c / SC_STAGES) & 1, abort_flag, err)) break;
+            float da8[CHUNK], ds8[CHUNK];
+#pragma unroll
+            for (int j = 0; j < CHUNK; j++) {
+                da8[j] = row_ok ? da[(int64_t)m * nb + c * CHUNK + j] : 0.0f;
+                if (has_offset(TYPE)) ds8[j] = row_ok ? ds[(int64_t)m * nb + c * CHUNK + j] : 0.0f;
+            }
+            const float *sc = sc_base + ss * L::SC_FLOATS;
+            bool ok = true;
+            for (int j = 0; j < CHUNK; j++) {
+                int kb = c * CHUNK + j, slot = kb % NSLOT;
+                if (!mbar_wait(t_full(slot), (kb / NSLOT) & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint32_t r[32];
+                    tmem_ld32(lane_addr + slot * BN + h * 32, r);
+                    if (DOTS) {
+                        if (row_ok) {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                int n = n0 + g * 64 + h * 32 + i;
+                                if (n < N) dots[((int64_t)m * N + n) * nb + kb] = (int32_t)__uint_as_float(r[i]);
+                            }
+                        }
+                    } else if (warp_live) {
+                        const float *dw = sc + j * BN + g * 64 + h * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            float s = __fmul_rn(dw[i], da8[j]);
+                            f[h * 32 + i] = __fmaf_rn(__uint_as_float(r[i]), s, f[h * 32 + i]);
+                        }
+                        if (has_offset(TYPE)) {
+                            const float *mo = sc + CHUNK * BN + j * BN + g * 64 + h * 32;
+#pragma unroll
+                            for (int i = 0; i < 32; i++) f[h * 32 + i] = __fmaf_rn(mo[i], ds8[j], f[h * 32 + i]);
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(t_empty(slot));
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sc_empty(ss));
+        }
+        if (!DOTS && row_ok && !*abort_flag) {
+            float *dst = y + (int64_t)m * ldy + n0 + g * 64;
+#pragma unroll
+            for (int i = 0; i < 64; i += 4) {
+                if (n0 + g * 64 + i >= N) break;
+                float4 v = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+                if (EPI == EPI_ADD) {
+                    float4 o = *reinterpret_cast<float4 *>(dst + i);
+                    v.x = __fadd_rn(o.x, v.x);
+                    v.y = __fadd_rn(o.y, v.y);
+                    v.z = __fadd_rn(o.z, v.z);
+                    v.w = __fadd_rn(o.w, v.w);
+                }
+                *reinterpret_cast<float4 *>(dst + i) = v;
+            }
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(NSLOT * BN));
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// Activations: f16 [M][K], box 64 x 128 rows, 128B swizzle.
+static bool map_activations(CUtensorMap *m, const __half *a, int64_t M, int64_t K) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+    cuuint32_t box[2] = {64, BM};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)a, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Raw weights: rows of 16-bit units, box = one 8-block chunk x 128 rows.
+static bool map_weights(CUtensorMap *m, const DevWeight &w, int raw_row) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)(w.row_bytes / 2), (cuuint64_t)w.rows};
+    cuuint64_t strides[1] = {(cuuint64_t)w.row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(raw_row / 2), BN};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)w.data, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int TYPE, int EPI, bool DOTS>
+static cudaError_t launch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+                            cudaStream_t s) {
+    using L = Smem<TYPE>;
+    CUtensorMap ma, mw;
+    if (!map_activations(&ma, q.a16, q.M, w.cols) || !map_weights(&mw, w, L::RAW_ROW)) return cudaErrorInvalidValue;
+    auto kern = k_gemm_tc<TYPE, EPI, DOTS>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((w.rows + BN - 1) / BN), (unsigned)((q.M + BM - 1) / BM));
+    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, q.da, q.ds, y, ldy, (int)q.M, (int)w.rows, (int)(w.cols / 32), err,
+                                         dots);
+    return cudaGetLastError();
+}
+
+template <int EPI, bool DOTS>
+static cudaError_t dispatch(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+                            cudaStream_t s) {
+    switch (w.type) {
+    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace tc
+
+bool gemm_tc_supports(const DevWeight &w, int64_t M) {
+    if (!block_bytes(w.type) || w.cols % 256 || w.rows % 16 || M < 1 || M > (1LL << 31) - 1) return false;
+    if (w.row_bytes % 16 || reinterpret_cast<uintptr_t>(w.data) % 16) return false;
+    if (w.rows / tc::BN > 65535 || (M + tc::BM - 1) / tc::BM > 65535) return false;
+    return tc::encode_fn() != nullptr;
+}
 
 cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
                            cudaStream_t s) {
-    return cudaErrorNotSupported;
+    if (!gemm_tc_supports(w, q.M) || !q.a16 || ldy % 4 || reinterpret_cast<uintptr_t>(y) % 16 ||
+        reinterpret_cast<uintptr_t>(q.a16) % 16)
+        return cudaErrorNotSupported;
+    if (q.M == 0) return cudaSuccess;
+    return epi == EPI_ADD ? tc::dispatch<EPI_ADD, false>(w, q, y, ldy, err, nullptr, s)
+                          : tc::dispatch<EPI_STORE, false>(w, q, y, ldy, err, nullptr, s);
 }
 
 cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s) {
-    return cudaErrorNotSupported;
+    if (!gemm_tc_supports(w, q.M) || !q.a16) return cudaErrorNotSupported;
+    return tc::dispatch<EPI_STORE, true>(w, q, nullptr, 0, err, dots, s);
 }
 
 }  // namespace shield
