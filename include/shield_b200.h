@@ -143,6 +143,31 @@ shield_status shield_qmatmul(shield_ctx *ctx, int32_t device, const char *weight
 shield_status shield_qmatmul_device(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x,
                                     int64_t M, float *d_y);
 
+/*
+ * shield_qmatmul_device for callers that cannot allocate GPU memory while they
+ * run: hosts that hand the GPU's memory to their own pool or arena up front,
+ * real-time services that forbid allocation on the request path, and
+ * embedders whose allocator is not CUDA's.  The other GEMM entry points
+ * allocate their activation scratch on first use and grow it with the
+ * problem size; this one allocates nothing, ever.  It has no counterpart in
+ * the reference, whose managed code rents its buffers from an ArrayPool.
+ *
+ * The scratch (the activations quantized to int8 and f16, their block
+ * scales and sums, an error word) is one fixed device array of about 6.8 MB
+ * that every GPU loading the library holds until the process exits, so
+ *   M * cols <= SHIELD_NOALLOC_MAX_ELEMENTS (2^21)
+ * and larger calls fail with SHIELD_ERR_ARG before touching the GPU.
+ * d_x (M x cols f32) and d_y (M x rows f32) are the caller's device buffers.
+ * The first call on a GPU looks up the array's device address for that GPU;
+ * make that first call before any stream capture.  All calls on a GPU share
+ * the one array and it keeps the last call's contents: calls that may
+ * overlap on the GPU (other host threads, other contexts) race and must be
+ * serialized by the caller.  The call returns after its work completes.
+ */
+#define SHIELD_NOALLOC_MAX_ELEMENTS (1 << 21)
+shield_status shield_qmatmul_noalloc(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x,
+                                     int64_t M, float *d_y);
+
 /* The raw per-block int32 dot products i = -z*Σa + Σ u*a of the integer GEMM
  * (IntegerGemm.cs:384-397): dots[(t*rows + n)*(cols/32) + b], for checking
  * bit-exactness.  path: 0 = the GEMM path shield_qmatmul would take,

@@ -54,7 +54,8 @@ class ShieldTiming(C.Structure):
 
 EXPORTS = [
     "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
-    "shield_score_batch", "shield_qmatmul", "shield_qmatmul_device", "shield_debug_block_dots",
+    "shield_score_batch", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
+    "shield_debug_block_dots",
     "shield_set_gemm_path", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
     "shield_device_stream", "shield_last_error",
 ]
@@ -80,6 +81,7 @@ def lib() -> C.CDLL:
         L.shield_score_batch.argtypes = [P, P, P, C.c_int32, P, C.c_int32, C.c_int32, P, P, P, P, P]
         L.shield_qmatmul.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, P, C.c_int32]
         L.shield_qmatmul_device.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
+        L.shield_qmatmul_noalloc.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
         L.shield_debug_block_dots.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, C.c_int32]
         L.shield_set_gemm_path.argtypes = [P, C.c_int32]
         L.shield_debug_activation.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_int32, P]
@@ -200,6 +202,10 @@ class ShieldContext:
 
     def qmatmul_device(self, weight: str, d_x: int, M: int, d_y: int, device: int = 0):
         _check(lib().shield_qmatmul_device(self._h, device, weight.encode(), C.c_void_p(d_x), M, C.c_void_p(d_y)))
+
+    def qmatmul_noalloc(self, weight: str, d_x: int, M: int, d_y: int, device: int = 0):
+        """shield_qmatmul_noalloc: the GEMM on device buffers, allocating nothing."""
+        _check(lib().shield_qmatmul_noalloc(self._h, device, weight.encode(), C.c_void_p(d_x), M, C.c_void_p(d_y)))
 
     def block_dots(self, weight: str, x: np.ndarray, M: int, rows: int, cols: int, path: int = 0, device: int = 0):
         x = np.ascontiguousarray(x, np.float32)

@@ -890,6 +890,28 @@ shield_status shield_qmatmul_device(shield_ctx *ctx, int32_t device, const char 
     });
 }
 
+shield_status shield_qmatmul_noalloc(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x,
+                                     int64_t M, float *d_y) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        Ctx &C = ctx->c;
+        Device &d = device_of(C, device);
+        const Tensor &W = matrix(d, weight);
+        if (M < 0) throw Error(SHIELD_ERR_ARG, "negative size");
+        if (M == 0) return;
+        if (!d_x || !d_y) throw Error(SHIELD_ERR_ARG, "x and y must be non-null");
+        if (M * W.w.cols > noalloc_max_elements())
+            throw Error(SHIELD_ERR_ARG, "M * cols = " + std::to_string(M * W.w.cols) +
+                                            " exceeds the no-allocation scratch limit of " +
+                                            std::to_string(noalloc_max_elements()) + " activation elements");
+        int32_t err = 0;
+        cudaError_t e = launch_qmatmul_noalloc(W.w, d_x, M, d_y, C.gemm_path, &err, d.stream);
+        if (e == cudaErrorNotSupported) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
+        check_launch(e, "no-allocation GEMM");
+        if (err) throw Error(SHIELD_ERR_TIMEOUT, "a device-side wait gave up (error word " + std::to_string(err) + ")");
+    });
+}
+
 shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const char *weight, const float *x, int64_t M,
                                       int32_t *dots, int32_t path) {
     return guarded([&] {

@@ -65,6 +65,12 @@ bool gemm_tc_supports(const DevWeight &w, int64_t M);
 cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s);
 cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s);
 
+// The GEMM with its activation scratch in a fixed device array (noalloc.cu);
+// synchronizes s and returns the kernel's error word in *err_out.
+cudaError_t launch_qmatmul_noalloc(const DevWeight &w, const float *x, int64_t M, float *y, int path,
+                                   int32_t *err_out, cudaStream_t s);
+int64_t noalloc_max_elements();
+
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, cudaStream_t s);
 cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, const int32_t *tok_start,
