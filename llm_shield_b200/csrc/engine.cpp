@@ -134,6 +134,10 @@ struct Buffers {
     float *da = nullptr, *ds = nullptr;
     int32_t *sums = nullptr;
     int32_t *meta = nullptr;   // ids | pos | tok_start | last  (4 * cap)
+    float *scores = nullptr;   // attention scores of a request group
+    int64_t scores_cap = 0;    // floats
+    int32_t *att = nullptr;    // attention work list | request start | len | base  (8 * cap int32)
+    int32_t *h_att = nullptr;  // pinned
     float *logits = nullptr;
     int32_t *verdict = nullptr;
     int32_t *err = nullptr;
@@ -142,7 +146,10 @@ struct Buffers {
     void free_all() {
         dev_free(h); dev_free(q); dev_free(k); dev_free(v); dev_free(ctx); dev_free(g); dev_free(u);
         dev_free(a8); dev_free(a16); dev_free(da); dev_free(ds); dev_free(sums); dev_free(meta);
-        dev_free(logits); dev_free(verdict); dev_free(err);
+        dev_free(logits); dev_free(verdict); dev_free(err); dev_free(scores); dev_free(att);
+        if (h_att) cudaFreeHost(h_att);
+        h_att = nullptr;
+        scores_cap = 0;
         if (h_meta) cudaFreeHost(h_meta);
         if (h_logits) cudaFreeHost(h_logits);
         h_meta = nullptr;
@@ -318,6 +325,13 @@ static void ensure_buffers(Ctx &C, Device &d) {
     SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_meta, (size_t)(4 * T) * 4));
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_logits, (size_t)(T * 64) * 4));
+    // attention scores: at least one longest request, at most ~4 GiB beyond that
+    int64_t one = (int64_t)c.n_heads * c.max_positions * c.max_positions;
+    int64_t all = std::min<int64_t>((int64_t)1 << 30, (int64_t)c.n_heads * T * c.max_positions);
+    d.buf.scores_cap = std::max(one, all);
+    dev_alloc(d.buf.scores, (size_t)d.buf.scores_cap);
+    dev_alloc(d.buf.att, (size_t)(8 * T));
+    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_att, (size_t)(8 * T) * 4));
     d.buf.cap = T;
 }
 
@@ -371,8 +385,51 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         f1 = T.event();
         if (f0) cudaEventRecord(f0, s);
     }
-    const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_start = b.meta + 2 * M, *d_last = b.meta + 3 * M;
-    int max_len = *std::max_element(B.len.begin(), B.len.end());
+    const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_last = b.meta + 3 * M;
+
+    // attention: requests grouped so each group's S x S scores per head fit the
+    // scratch; one work item per (request, 128/G query tokens)
+    const int G = c.n_heads / c.n_kv_heads, QT = attention_rows_per_cta() / G;
+    struct AttGroup { int w0, nw; };
+    std::vector<AttGroup> groups;
+    std::vector<int32_t> work;
+    std::vector<int64_t> rbase(R);
+    {
+        int64_t used = 0;
+        AttGroup cur{0, 0};
+        for (int r = 0; r < R; r++) {
+            int64_t need = (int64_t)c.n_heads * B.len[r] * B.len[r];
+            if (used + need > b.scores_cap && cur.nw > 0) {
+                groups.push_back(cur);
+                cur = AttGroup{(int)(work.size() / 2), 0};
+                used = 0;
+            }
+            rbase[r] = used;
+            used += need;
+            for (int q0 = 0; q0 < B.len[r]; q0 += QT) {
+                work.push_back(r);
+                work.push_back(q0);
+                cur.nw++;
+            }
+        }
+        if (cur.nw > 0) groups.push_back(cur);
+    }
+    const int n_work = (int)(work.size() / 2);
+    if (2 * n_work + 4 * R > 8 * b.cap) throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
+    int32_t *ha = b.h_att;
+    memcpy(ha, work.data(), work.size() * 4);
+    int32_t *ha_start = ha + 2 * n_work, *ha_len = ha_start + R;
+    for (int r = 0; r < R; r++) {
+        ha_start[r] = (int32_t)B.start[r];
+        ha_len[r] = B.len[r];
+    }
+    int64_t base_off = (2 * n_work + 2 * R + 1) / 2 * 2;  // int64 array on an 8-byte boundary
+    memcpy(ha + base_off, rbase.data(), (size_t)R * 8);
+    size_t att_bytes = (size_t)(base_off + 2 * R) * 4;
+    SHIELD_CUDA(cudaMemcpyAsync(b.att, ha, att_bytes, cudaMemcpyHostToDevice, s));
+    const int2 *d_work = reinterpret_cast<const int2 *>(b.att);
+    const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R;
+    const int64_t *d_rbase = reinterpret_cast<const int64_t *>(b.att + base_off);
 
     const Tensor &emb = d.get("token_embd.weight");
     count_launch(d), check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
@@ -408,8 +465,12 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());
-        count_launch(d), check_launch(launch_attention(b.q, b.k, b.v, b.ctx, d_start, M, c.n_heads, c.n_kv_heads, c.head_dim, scale,
-                                      max_len, s), "attention");
+        for (const AttGroup &ag : groups) {
+            d.timing.launches += 3;
+            check_launch(launch_attention(b.q, b.k, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
+                                          d_rbase, c.n_heads, c.n_kv_heads, c.head_dim, scale, s),
+                         "attention");
+        }
         cap(l, SHIELD_ACT_ATTN_WEIGHTED, b.ctx, c.qdim());
         QAct qc = qact(b, M, c.qdim());
         count_launch(d), check_launch(launch_quantize(b.ctx, M, c.qdim(), c.qdim(), qc, s), "quantize context");
@@ -506,8 +567,8 @@ static void set_config(Ctx &C, const shield_config *in) {
                                           std::to_string(c.n_kv_heads) + " KV heads");
     if (c.hidden % 32 || c.ffn % 32 || (c.n_heads * c.head_dim) % 32)
         throw Error(SHIELD_ERR_UNSUPPORTED, "hidden, ffn and q dimensions must be multiples of 32");
-    if (c.head_dim % 8 || c.head_dim > 256 || c.n_heads / c.n_kv_heads > 32)
-        throw Error(SHIELD_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 up to 256, and at most 32 query heads per KV head");
+    if (c.head_dim != 128 || 128 % (c.n_heads / c.n_kv_heads))
+        throw Error(SHIELD_ERR_UNSUPPORTED, "the attention kernels take head_dim 128 and a power-of-two GQA group");
     Config cfg;
     cfg.n_layers = c.n_layers;
     cfg.hidden = c.hidden;
@@ -531,10 +592,6 @@ static void set_config(Ctx &C, const shield_config *in) {
     cfg.orig_ctx = c.rope_orig_ctx;
     cfg.max_positions = c.max_positions > 0 ? c.max_positions : 8192;
     cfg.max_batch_tokens = c.max_batch_tokens > 0 ? c.max_batch_tokens : 16384;
-    int group = c.n_heads / c.n_kv_heads;
-    int64_t att_smem = (int64_t)group * c.head_dim * 4 + (int64_t)group * cfg.max_positions * 4;
-    if (att_smem > 227 * 1024)
-        throw Error(SHIELD_ERR_UNSUPPORTED, "max_positions too long for the attention kernel's score buffer");
     if (cfg.max_batch_tokens < cfg.max_positions) cfg.max_batch_tokens = cfg.max_positions;
     C.cfg = cfg;
     C.configured = true;

@@ -42,88 +42,235 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
     return cudaGetLastError();
 }
 
-// Causal grouped-query attention (AttendGroup, MinistralModel.cs:372-440) for
-// one query token and one KV head: warp g handles query head kvh*group + g.
-// Scores follow Kernels.Dot4's order (8 lanes of fused multiply-adds, then
-// Vector.Sum), the softmax sums 32 lane-strided partials folded by a butterfly
-// and uses shield_expf (the oracle's order and exp), the context follows
-// AddScaled4 (a fused multiply-add chain over positions in order), so the
-// result is bit-identical to the oracle.
-// q: M x (H*hd), k/v: M x (KVH*hd), tok_start[t] = index of t's request start.
-__global__ void k_attention(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
-                            float *__restrict__ ctx, const int32_t *__restrict__ tok_start, int n_heads,
-                            int n_kv_heads, int head_dim, float scale) {
-    extern __shared__ float smem[];
-    const int group = n_heads / n_kv_heads;
-    const int64_t t = blockIdx.x;
-    const int kvh = blockIdx.y;
-    const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t start = tok_start[t];
-    const int limit = (int)(t - start + 1);
-    const int head = kvh * group + g;
-    const int64_t qdim = (int64_t)n_heads * head_dim, kvdim = (int64_t)n_kv_heads * head_dim;
-    float *qs = smem + g * head_dim;                        // this head's query
-    float *sc = smem + group * head_dim + (int64_t)g * limit;  // this head's scores
-    for (int d = lane; d < head_dim; d += 32) qs[d] = q[t * qdim + (int64_t)head * head_dim + d];
-    __syncwarp();
-    float mx = -INFINITY;
-    for (int p = lane; p < limit; p += 32) {
-        const float *kp = k + (start + p) * kvdim + (int64_t)kvh * head_dim;
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int i = 0; i + 8 <= head_dim; i += 8) {
-            float4 k0 = *reinterpret_cast<const float4 *>(kp + i);
-            float4 k1 = *reinterpret_cast<const float4 *>(kp + i + 4);
-            acc[0] = __fmaf_rn(qs[i + 0], k0.x, acc[0]);
-            acc[1] = __fmaf_rn(qs[i + 1], k0.y, acc[1]);
-            acc[2] = __fmaf_rn(qs[i + 2], k0.z, acc[2]);
-            acc[3] = __fmaf_rn(qs[i + 3], k0.w, acc[3]);
-            acc[4] = __fmaf_rn(qs[i + 4], k1.x, acc[4]);
-            acc[5] = __fmaf_rn(qs[i + 5], k1.y, acc[5]);
-            acc[6] = __fmaf_rn(qs[i + 6], k1.z, acc[6]);
-            acc[7] = __fmaf_rn(qs[i + 7], k1.w, acc[7]);
+// Causal grouped-query attention over a ragged batch (AttendGroup,
+// MinistralModel.cs:372-440), in three kernels that keep the oracle's exact
+// operation order, so the context is bit-identical to it:
+//   k_attn_scores   s = (Σ over 8 FMA chains, folded as Vector.Sum) * scale,
+//                   chain j = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4)
+//   k_attn_softmax  max, shield_expf(s - max), 32 lane-strided partial sums
+//                   folded pairwise, division (Kernels.Softmax)
+//   k_attn_pv       ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
+// One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
+// the G query heads sharing that KV head, so each key and value row is read
+// once per CTA for all of them. Scores live in a scratch buffer laid out per
+// request as [head][position][key] (S x S per head).
+namespace att {
+constexpr int R = 128;       // query rows per CTA
+constexpr int HD = 128;      // head_dim this kernel is written for
+constexpr int KT = 32;       // keys per tile
+constexpr int LD = HD + 4;   // padded row of a Q/K/V tile in shared memory
+constexpr int LDW = R + 4;   // padded row of a weight tile
+constexpr int THREADS = 256;
+}  // namespace att
+
+// dim d of a head stored so that FMA chain j (dims j, j+8, ...) is contiguous
+__device__ __forceinline__ int chain_pos(int d) { return (d & 7) * (att::HD / 8) + (d >> 3); }
+
+__global__ void __launch_bounds__(att::THREADS, 2)
+k_attn_scores(const float *__restrict__ q, const float *__restrict__ k, float *__restrict__ scores,
+              const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
+              const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads, float scale) {
+    using namespace att;
+    extern __shared__ float sm[];
+    float *Qs = sm;            // R x LD, chain-major dims
+    float *Ks = sm + R * LD;   // KT x LD
+    const int G = n_heads / n_kv_heads, QT = R / G;
+    const int2 wk = work[blockIdx.x];
+    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
+    const int S = req_len[r];
+    const int64_t start = req_start[r], base = req_base[r];
+    const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
+    const int tid = threadIdx.x;
+    for (int idx = tid; idx < R * HD; idx += THREADS) {
+        int row = idx / HD, d = idx % HD, i = row / G, g = row % G, tok = q0 + i;
+        Qs[row * LD + chain_pos(d)] = tok < S ? q[(start + tok) * qdim + (int64_t)(h * G + g) * HD + d] : 0.0f;
+    }
+    const int warp = tid >> 5, lane = tid & 31;
+    const int rl = lane >> 3, kl = lane & 7;  // rows warp*16 + rl + 4a, keys kl + 8b
+    const int qend = min(q0 + QT, S);
+    for (int kt0 = 0; kt0 < qend; kt0 += KT) {
+        __syncthreads();
+        for (int idx = tid; idx < KT * HD; idx += THREADS) {
+            int kk = idx / HD, d = idx % HD, p = kt0 + kk;
+            Ks[kk * LD + chain_pos(d)] = p < S ? k[(start + p) * kvdim + (int64_t)h * HD + d] : 0.0f;
         }
-        float s = __fmul_rn(vsum8(acc), scale);
-        sc[p] = s;
-        mx = fmaxf(mx, s);
-    }
-    mx = warp_max(mx);
-    float sum = 0.0f;
-    for (int p = lane; p < limit; p += 32) {
-        float e = shield_expf(__fsub_rn(sc[p], mx));
-        sc[p] = e;
-        sum = __fadd_rn(sum, e);
-    }
+        __syncthreads();
+        float e0[16], e4[16], T[16], U[16];
+        auto chain = [&](int j, float (&c)[16]) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-    __syncwarp();
-    for (int p = lane; p < limit; p += 32) sc[p] = __fdiv_rn(sc[p], sum);
-    __syncwarp();
-    for (int d = lane; d < head_dim; d += 32) {
-        float c = 0.0f;
-        const float *vp = v + start * kvdim + (int64_t)kvh * head_dim + d;
-        for (int p = 0; p < limit; p++) {
-            float w = sc[p];
-            if (w != 0.0f) c = __fmaf_rn(vp[(int64_t)p * kvdim], w, c);
+            for (int o = 0; o < 16; o++) c[o] = 0.0f;
+#pragma unroll
+            for (int st = 0; st < HD / 8; st += 4) {
+                float4 qa[4], kb[4];
+#pragma unroll
+                for (int a = 0; a < 4; a++)
+                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * (HD / 8) + st]);
+#pragma unroll
+                for (int b = 0; b < 4; b++)
+                    kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * (HD / 8) + st]);
+#pragma unroll
+                for (int a = 0; a < 4; a++)
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        float &acc = c[a * 4 + b];
+                        acc = __fmaf_rn(qa[a].x, kb[b].x, acc);
+                        acc = __fmaf_rn(qa[a].y, kb[b].y, acc);
+                        acc = __fmaf_rn(qa[a].z, kb[b].z, acc);
+                        acc = __fmaf_rn(qa[a].w, kb[b].w, acc);
+                    }
+            }
+        };
+        // Vector.Sum order: ((e0+e4)+(e1+e5)) + ((e2+e6)+(e3+e7))
+        chain(0, e0);
+        chain(4, e4);
+#pragma unroll
+        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(e0[o], e4[o]);
+        chain(1, e0);
+        chain(5, e4);
+#pragma unroll
+        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(T[o], __fadd_rn(e0[o], e4[o]));
+        chain(2, e0);
+        chain(6, e4);
+#pragma unroll
+        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(e0[o], e4[o]);
+        chain(3, e0);
+        chain(7, e4);
+#pragma unroll
+        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(e0[o], e4[o]));
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+            const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, pt = q0 + i;
+            if (pt >= S) continue;
+            float *dst = scores + base + ((int64_t)(h * G + g) * S + pt) * S;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int p = kt0 + kl + 8 * b;
+                if (p <= pt) dst[p] = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), scale);
+            }
         }
-        ctx[t * qdim + (int64_t)head * head_dim + d] = c;
     }
 }
 
-cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, const int32_t *tok_start,
-                             int64_t M, int n_heads, int n_kv_heads, int head_dim, float scale, int max_len,
-                             cudaStream_t s) {
-    if (M == 0) return cudaSuccess;
-    int group = n_heads / n_kv_heads;
-    size_t smem = (size_t)group * head_dim * 4 + (size_t)group * max_len * 4;
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
+// One warp per row at a time: rows of the CTA's 128-row tile, in turn.
+__global__ void __launch_bounds__(att::THREADS)
+k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const int32_t *__restrict__ req_len,
+               const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads) {
+    using namespace att;
+    const int G = n_heads / n_kv_heads, QT = R / G;
+    const int2 wk = work[blockIdx.x];
+    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
+    const int S = req_len[r];
+    const int64_t base = req_base[r];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qend = min(q0 + QT, S);
+    for (int row = warp; row < R; row += THREADS / 32) {
+        const int i = row / G, g = row % G, pt = q0 + i;
+        if (pt >= S) continue;
+        const int limit = pt + 1;
+        float *s = scores + base + ((int64_t)(h * G + g) * S + pt) * S;
+        float mx = -INFINITY;
+        for (int p = lane; p < limit; p += 32) mx = fmaxf(mx, s[p]);
+        mx = warp_max(mx);
+        float sum = 0.0f;
+        for (int p = lane; p < limit; p += 32) {
+            float e = shield_expf(__fsub_rn(s[p], mx));
+            s[p] = e;
+            sum = __fadd_rn(sum, e);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        __syncwarp();
+        for (int p = lane; p < limit; p += 32) s[p] = __fdiv_rn(s[p], sum);
+        for (int p = limit + lane; p < qend; p += 32) s[p] = 0.0f;  // keys the PV tile walks past
+        __syncwarp();
     }
-    dim3 grid((unsigned)M, (unsigned)n_kv_heads);
-    k_attention<<<grid, group * 32, smem, s>>>(q, k, v, ctx, tok_start, n_heads, n_kv_heads, head_dim, scale);
+}
+
+__global__ void __launch_bounds__(att::THREADS, 2)
+k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *__restrict__ ctx,
+          const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
+          const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads) {
+    using namespace att;
+    extern __shared__ float sm[];
+    float *Vs = sm;             // KT x LD
+    float *Ws = sm + KT * LD;   // KT x LDW  (key-major: the 128 rows' weights of one key)
+    const int G = n_heads / n_kv_heads, QT = R / G;
+    const int2 wk = work[blockIdx.x];
+    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
+    const int S = req_len[r];
+    const int64_t start = req_start[r], base = req_base[r];
+    const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
+    const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;  // rows tr*4.., dims td*4 + 32e ..
+    const int qend = min(q0 + QT, S);
+    float c[4][16];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int e = 0; e < 16; e++) c[a][e] = 0.0f;
+    for (int kt0 = 0; kt0 < qend; kt0 += KT) {
+        __syncthreads();
+        for (int idx = tid; idx < KT * HD; idx += THREADS) {
+            int kk = idx / HD, d = idx % HD, p = kt0 + kk;
+            Vs[kk * LD + d] = p < qend ? v[(start + p) * kvdim + (int64_t)h * HD + d] : 0.0f;
+        }
+        for (int idx = tid; idx < R * KT; idx += THREADS) {
+            int row = idx / KT, kk = idx % KT, p = kt0 + kk, i = row / G, g = row % G, pt = q0 + i;
+            float w = 0.0f;
+            if (pt < S && p < qend) w = scores[base + ((int64_t)(h * G + g) * S + pt) * S + p];
+            Ws[kk * LDW + row] = w;
+        }
+        __syncthreads();
+        const int kn = min(KT, qend - kt0);
+        for (int kk = 0; kk < kn; kk++) {
+            const float4 w = *reinterpret_cast<const float4 *>(&Ws[kk * LDW + tr * 4]);
+            const float wr[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float4 vv = *reinterpret_cast<const float4 *>(&Vs[kk * LD + td * 4 + 32 * e]);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    c[a][4 * e + 0] = __fmaf_rn(vv.x, wr[a], c[a][4 * e + 0]);
+                    c[a][4 * e + 1] = __fmaf_rn(vv.y, wr[a], c[a][4 * e + 1]);
+                    c[a][4 * e + 2] = __fmaf_rn(vv.z, wr[a], c[a][4 * e + 2]);
+                    c[a][4 * e + 3] = __fmaf_rn(vv.w, wr[a], c[a][4 * e + 3]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        const int row = tr * 4 + a, i = row / G, g = row % G, pt = q0 + i;
+        if (pt >= S) continue;
+        float *dst = ctx + (start + pt) * qdim + (int64_t)(h * G + g) * HD;
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            *reinterpret_cast<float4 *>(dst + td * 4 + 32 * e) =
+                make_float4(c[a][4 * e], c[a][4 * e + 1], c[a][4 * e + 2], c[a][4 * e + 3]);
+    }
+}
+
+cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, float *scores,
+                             const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
+                             const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
+                             cudaStream_t s) {
+    using namespace att;
+    if (n_work == 0) return cudaSuccess;
+    if (head_dim != HD || n_heads % n_kv_heads || R % (n_heads / n_kv_heads)) return cudaErrorInvalidValue;
+    const size_t smem_s = (size_t)(R + KT) * LD * 4, smem_pv = (size_t)KT * (LD + LDW) * 4;
+    cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)n_work, (unsigned)n_kv_heads);
+    k_attn_scores<<<grid, THREADS, smem_s, s>>>(q, k, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
+                                                 scale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_attn_softmax<<<grid, THREADS, 0, s>>>(scores, work, req_len, req_base, n_heads, n_kv_heads);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_attn_pv<<<grid, THREADS, smem_pv, s>>>(v, scores, ctx, work, req_start, req_len, req_base, n_heads,
+                                             n_kv_heads);
     return cudaGetLastError();
 }
+
+int attention_rows_per_cta() { return att::R; }
 
 // Kernels.SwiGlu (Kernels.cs:83-90): u = g*u; g = sigmoid(g)*u, in place in g.
 __global__ void k_swiglu(float *__restrict__ g, float *__restrict__ u, int64_t n) {

@@ -18,7 +18,7 @@
 //               f16 integers in the canonical SW128 K-major layout; widen the
 //               f16 block scales (and offsets) to f32
 //   warps 4-11  epilogue: tcgen05.ld the slot, apply the block's f32 scaling
-//               chain per output, write (or add to) y
+//               chain per output (packed f32x2 operations), write or add to y
 //
 // kind::f16 rather than kind::i8: products of 8-bit integers summed over one
 // block stay below 2^20, so the f32 accumulator holds the exact int32 sum and
@@ -40,8 +40,9 @@ constexpr int RAW_STAGES = 2;    // raw weight chunks in flight
 constexpr int SC_STAGES = 2;     // f32 scale chunks in flight
 constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns)
 constexpr int CHUNK = 8;         // blocks per raw chunk (TMA inner box = 8 blocks)
-constexpr int THREADS = 384;
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 8;              // warp e owns lane quarter e%4 and columns EPI_COLS*(e/4)..
+constexpr int EPI_COLS = BN / (EPI_WARPS / 4);
+constexpr int THREADS = 128 + 32 * EPI_WARPS;
 constexpr int UNPACK_THREADS = 64;
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -156,6 +157,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Two independent IEEE f32 operations per instruction (sm_100 packed f32x2):
+// each lane rounds exactly as the scalar __fmul_rn / __fmaf_rn would.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
 }
 
 // ------------------------------------------------------------ unpacking
@@ -363,27 +380,36 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         }
     } else {
         // ------------------------------------------------------ epilogue
-        const int q = warp & 3;              // TMEM lane quarter this warp may access
-        const int g = (warp - 4) >> 2;       // column half (0: 0..63, 1: 64..127)
-        const int t = q * 32 + lane;         // token within the tile
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int g = (warp - 4) >> 2;          // column group: columns g*EPI_COLS ..
+        const int t = q * 32 + lane;            // token within the tile
         const int m = m0 + t;
         const bool row_ok = m < M;
         const bool warp_live = m0 + q * 32 < M;
-        float f[64];
+        uint64_t f[EPI_COLS / 2];  // this thread's outputs as f32 pairs
 #pragma unroll
-        for (int i = 0; i < 64; i++) f[i] = 0.0f;
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * 64;
+        for (int i = 0; i < EPI_COLS / 2; i++) f[i] = 0;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
+        // this token's activation scales for the current chunk, the next chunk's in flight
+        float da8[CHUNK], ds8[CHUNK];
+#pragma unroll
+        for (int j = 0; j < CHUNK; j++) {
+            da8[j] = row_ok ? da[(int64_t)m * nb + j] : 0.0f;
+            if (has_offset(TYPE)) ds8[j] = row_ok ? ds[(int64_t)m * nb + j] : 0.0f;
+        }
         for (int c = 0; c < nchunks; c++) {
             int ss = c % SC_STAGES;
-            if (!mbar_wait(sc_full(ss), (c / SC_STAGES) & 1, abort_flag, err)) break;
-            float da8[CHUNK], ds8[CHUNK];
+            float dn8[CHUNK], sn8[CHUNK];
+            const bool more = row_ok && c + 1 < nchunks;
 #pragma unroll
             for (int j = 0; j < CHUNK; j++) {
-                da8[j] = row_ok ? da[(int64_t)m * nb + c * CHUNK + j] : 0.0f;
-                if (has_offset(TYPE)) ds8[j] = row_ok ? ds[(int64_t)m * nb + c * CHUNK + j] : 0.0f;
+                dn8[j] = more ? da[(int64_t)m * nb + (c + 1) * CHUNK + j] : 0.0f;
+                if (has_offset(TYPE)) sn8[j] = more ? ds[(int64_t)m * nb + (c + 1) * CHUNK + j] : 0.0f;
             }
+            if (!mbar_wait(sc_full(ss), (c / SC_STAGES) & 1, abort_flag, err)) break;
             const float *sc = sc_base + ss * L::SC_FLOATS;
             bool ok = true;
+#pragma unroll 1
             for (int j = 0; j < CHUNK; j++) {
                 int kb = c * CHUNK + j, slot = kb % NSLOT;
                 if (!mbar_wait(t_full(slot), (kb / NSLOT) & 1, abort_flag, err)) {
@@ -391,29 +417,41 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     break;
                 }
                 tc_fence_after();
+                const uint64_t da2 = pack2(da8[j], da8[j]);
+                const uint64_t ds2 = has_offset(TYPE) ? pack2(ds8[j], ds8[j]) : 0;
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
+                for (int h = 0; h < EPI_COLS / 32; h++) {
                     uint32_t r[32];
                     tmem_ld32(lane_addr + slot * BN + h * 32, r);
                     if (DOTS) {
                         if (row_ok) {
 #pragma unroll
                             for (int i = 0; i < 32; i++) {
-                                int n = n0 + g * 64 + h * 32 + i;
+                                int n = n0 + g * EPI_COLS + h * 32 + i;
                                 if (n < N) dots[((int64_t)m * N + n) * nb + kb] = (int32_t)__uint_as_float(r[i]);
                             }
                         }
                     } else if (warp_live) {
-                        const float *dw = sc + j * BN + g * 64 + h * 32;
+                        const float4 *dw4 = reinterpret_cast<const float4 *>(sc + j * BN + g * EPI_COLS + h * 32);
 #pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            float s = __fmul_rn(dw[i], da8[j]);
-                            f[h * 32 + i] = __fmaf_rn(__uint_as_float(r[i]), s, f[h * 32 + i]);
+                        for (int i = 0; i < 8; i++) {
+                            const float4 w = dw4[i];
+                            const int p = h * 16 + 2 * i;
+                            f[p] = fma2(pack2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                        mul2(pack2(w.x, w.y), da2), f[p]);
+                            f[p + 1] = fma2(pack2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                            mul2(pack2(w.z, w.w), da2), f[p + 1]);
                         }
                         if (has_offset(TYPE)) {
-                            const float *mo = sc + CHUNK * BN + j * BN + g * 64 + h * 32;
+                            const float4 *mo4 =
+                                reinterpret_cast<const float4 *>(sc + CHUNK * BN + j * BN + g * EPI_COLS + h * 32);
 #pragma unroll
-                            for (int i = 0; i < 32; i++) f[h * 32 + i] = __fmaf_rn(mo[i], ds8[j], f[h * 32 + i]);
+                            for (int i = 0; i < 8; i++) {
+                                const float4 o = mo4[i];
+                                const int p = h * 16 + 2 * i;
+                                f[p] = fma2(pack2(o.x, o.y), ds2, f[p]);
+                                f[p + 1] = fma2(pack2(o.z, o.w), ds2, f[p + 1]);
+                            }
                         }
                     }
                 }
@@ -424,13 +462,20 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(sc_empty(ss));
+#pragma unroll
+            for (int j = 0; j < CHUNK; j++) {
+                da8[j] = dn8[j];
+                if (has_offset(TYPE)) ds8[j] = sn8[j];
+            }
         }
         if (!DOTS && row_ok && !*abort_flag) {
-            float *dst = y + (int64_t)m * ldy + n0 + g * 64;
+            float *dst = y + (int64_t)m * ldy + n0 + g * EPI_COLS;
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
-                if (n0 + g * 64 + i >= N) break;
-                float4 v = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+            for (int i = 0; i < EPI_COLS; i += 4) {
+                if (n0 + g * EPI_COLS + i >= N) break;
+                float4 v = make_float4(__uint_as_float((uint32_t)f[i / 2]), __uint_as_float((uint32_t)(f[i / 2] >> 32)),
+                                       __uint_as_float((uint32_t)f[i / 2 + 1]),
+                                       __uint_as_float((uint32_t)(f[i / 2 + 1] >> 32)));
                 if (EPI == EPI_ADD) {
                     float4 o = *reinterpret_cast<float4 *>(dst + i);
                     v.x = __fadd_rn(o.x, v.x);

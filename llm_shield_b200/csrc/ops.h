@@ -73,9 +73,15 @@ int64_t noalloc_max_elements();
 
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, cudaStream_t s);
-cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, const int32_t *tok_start,
-                             int64_t M, int n_heads, int n_kv_heads, int head_dim, float scale, int max_len,
+// Causal GQA attention of a group of requests (three kernels, see forward_ops.cu).
+// work[i] = {request, first query token}; one CTA per (work item, KV head)
+// covers attention_rows_per_cta() query rows (tokens x the heads of a group).
+// scores: scratch of n_heads * Σ len² floats, request r at req_base[r].
+cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, float *scores,
+                             const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
+                             const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s);
+int attention_rows_per_cta();
 cudaError_t launch_swiglu(float *g, float *u, int64_t n, cudaStream_t s);
 
 }  // namespace shield

@@ -836,9 +836,12 @@ static void orc_attend(void *vctx, int64_t item) {
         orc_softmax(s, limit);
         float *ch = J->ctx + (int64_t)t * qdim + (int64_t)head * hd;
         for (int d = 0; d < hd; d++) ch[d] = 0.0f;
+        /* AddScaled4 for every position. The reference skips a position only when
+         * all four heads' weights are exactly zero (MinistralModel.cs:422);
+         * fma(v, 0, c) == c for finite v except that it may turn a -0 context
+         * into +0, so the skip changes no value beyond the sign of a zero. */
         for (int p = 0; p < limit; p++) {
             float w = s[p];
-            if (w == 0.0f) continue;
             const float *vp = J->values + (int64_t)p * kvdim + (int64_t)kvh * hd;
             for (int d = 0; d < hd; d++) ch[d] = fmaf(vp[d], w, ch[d]); /* Kernels.AddScaled4 */
         }
