@@ -176,8 +176,12 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
                                       int64_t M, int32_t *dots, int32_t path);
 
 /* Which GEMM kernel the context uses: 0 = automatic (tensor cores where the
- * shape allows), 1 = CUDA-core kernel only, 2 = tensor cores only (shapes they
- * do not take fail with SHIELD_ERR_UNSUPPORTED). For cross-checking. */
+ * shape allows; long token batches read a once-unpacked f16 copy of the
+ * layer weights, short ones unpack the GGUF blocks on the fly), 1 = CUDA-core
+ * kernel only, 2 = tensor cores unpacking GGUF blocks only, 3 = tensor cores
+ * on the unpacked copy only. 2 and 3 fail with SHIELD_ERR_UNSUPPORTED on shapes
+ * the tensor cores do not take; the raw/unpacked choice is process-wide.
+ * For cross-checking the kernels against each other. */
 shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path);
 
 /* Intermediate tensors of one layer, named as MinistralModel's

@@ -225,6 +225,7 @@ struct Device {
             if (kv.second.vec) cudaFree(kv.second.vec);
             if (kv.second.w.scale_plane) cudaFree(kv.second.w.scale_plane);
             if (kv.second.w.offset_plane) cudaFree(kv.second.w.offset_plane);
+            if (kv.second.w.w16) cudaFree(kv.second.w.w16);
         }
         dev_free(cos_t);
         dev_free(sin_t);
@@ -272,7 +273,7 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
             check_launch(e, "tensor-core GEMM");
     }
     if (!done) {
-        if (C.gemm_path == 2) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
+        if (C.gemm_path >= 2) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
         check_launch(launch_gemm_simt(W.w, nullptr, W.w.rows, q, y, ldy, epi, d.stream), "CUDA-core GEMM");
     }
     count_launch(d);
@@ -631,6 +632,7 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
             if (old->second.vec) cudaFree(old->second.vec);
             if (old->second.w.scale_plane) cudaFree(old->second.w.scale_plane);
             if (old->second.w.offset_plane) cudaFree(old->second.w.offset_plane);
+            if (old->second.w.w16) cudaFree(old->second.w.w16);
             d.tensors.erase(old);
         }
         Tensor t;
@@ -659,6 +661,12 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
             dev_alloc(t.w.scale_plane, (size_t)(rows * (cols / 32)));
             if (type == T_Q4_1 || type == T_Q5_1) dev_alloc(t.w.offset_plane, (size_t)(rows * (cols / 32)));
             check_launch(launch_build_planes(t.w, nullptr), "scale planes");
+            // layer matrices also get an f16 copy for long token batches (the tied
+            // embedding/head is only ever read a few rows at a time)
+            if (n.compare(0, 4, "blk.") == 0 && cols % 256 == 0 && rows % 16 == 0) {
+                dev_alloc(t.w.w16, (size_t)(rows * cols));
+                check_launch(launch_unpack_f16(t.w, nullptr), "f16 weight copy");
+            }
             SHIELD_CUDA(cudaDeviceSynchronize());
         }
         d.tensors.emplace(n, t);
@@ -1003,8 +1011,9 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
 shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path) {
     return guarded([&] {
         if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
-        if (path < 0 || path > 2) throw Error(SHIELD_ERR_ARG, "path must be 0, 1 or 2");
+        if (path < 0 || path > 3) throw Error(SHIELD_ERR_ARG, "path must be 0, 1, 2 or 3");
         ctx->c.gemm_path = path;
+        gemm_tc_set_pre_min_tokens(path == 2 ? INT64_MAX : path == 3 ? 1 : -1);
     });
 }
 

@@ -146,6 +146,20 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -228,9 +242,13 @@ __device__ __forceinline__ void unpack_block(const uint8_t *blk, uint32_t (&o)[1
 
 // ------------------------------------------------------------------ kernel
 
-template <int TYPE, int EPI, bool DOTS>
+// PRE: the weights come pre-unpacked (f16 copy) and their scales from the f32
+// planes, both by TMA; the unpacker warps then idle.
+template <int TYPE, int EPI, bool DOTS, bool PRE>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+          const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_sc,
+          const __grid_constant__ CUtensorMap map_off,
           const float *__restrict__ da, const float *__restrict__ ds, float *__restrict__ y, int64_t ldy, int M, int N,
           int nb, int32_t *__restrict__ err, int32_t *__restrict__ dots) {
     using L = Smem<TYPE>;
@@ -267,7 +285,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             mbar_init(raw_empty(s), UNPACK_THREADS);
         }
         for (int s = 0; s < SC_STAGES; s++) {
-            mbar_init(sc_full(s), UNPACK_THREADS);
+            mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS);
             mbar_init(sc_empty(s), EPI_WARPS);
         }
         for (int s = 0; s < NSLOT; s++) {
@@ -293,16 +311,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         if (lane == 0) {
             for (int p = 0; p < npairs; p++) {
                 if ((2 * p) % CHUNK == 0) {
-                    int c = (2 * p) / CHUNK, rs = c % RAW_STAGES;
-                    if (!mbar_wait(raw_empty(rs), ((c / RAW_STAGES) & 1) ^ 1, abort_flag, err)) break;
-                    mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
-                    tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w, c * (L::RAW_ROW / 2),
-                                n0, raw_full(rs));
+                    int c = (2 * p) / CHUNK;
+                    if (PRE) {
+                        int ss = c % SC_STAGES;
+                        if (!mbar_wait(sc_empty(ss), ((c / SC_STAGES) & 1) ^ 1, abort_flag, err)) break;
+                        mbar_expect_tx(sc_full(ss), L::SC_FLOATS * 4);
+                        uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
+                        tma_load_2d(dst, &map_sc, n0, c * CHUNK, sc_full(ss));
+                        if (has_offset(TYPE)) tma_load_2d(dst + CHUNK * BN * 4, &map_off, n0, c * CHUNK, sc_full(ss));
+                    } else {
+                        int rs = c % RAW_STAGES;
+                        if (!mbar_wait(raw_empty(rs), ((c / RAW_STAGES) & 1) ^ 1, abort_flag, err)) break;
+                        mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
+                        tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w,
+                                    c * (L::RAW_ROW / 2), n0, raw_full(rs));
+                    }
                 }
                 int s = p % STAGES;
                 if (!mbar_wait(a_empty(s), ((p / STAGES) & 1) ^ 1, abort_flag, err)) break;
-                mbar_expect_tx(a_full(s), L::A_BYTES);
+                mbar_expect_tx(a_full(s), L::A_BYTES + (PRE ? L::B_BYTES : 0));
                 tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &map_a, 2 * p * 32, m0, a_full(s));
+                if (PRE) tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &map_b, 2 * p * 32, n0, a_full(s));
             }
         }
     } else if (warp == 1) {
@@ -312,7 +341,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 int s = p % STAGES;
                 uint32_t ph = (p / STAGES) & 1;
                 if (!mbar_wait(a_full(s), ph, abort_flag, err)) break;
-                if (!mbar_wait(b_full(s), ph, abort_flag, err)) break;
+                if (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err)) break;
                 tc_fence_after();
                 bool ok = true;
                 for (int jb = 0; jb < 2; jb++) {
@@ -332,11 +361,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 }
                 if (!ok) break;
                 umma_commit(a_empty(s));
-                umma_commit(b_empty(s));
+                if (!PRE) umma_commit(b_empty(s));
             }
         }
     } else if (warp < 4) {
         // ------------------------------------------------------ unpackers
+        if (PRE) goto done;
         const int ut = threadIdx.x - 64;
         for (int c = 0; c < nchunks; c++) {
             int rs = c % RAW_STAGES, ss = c % SC_STAGES;
@@ -487,6 +517,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             }
         }
     }
+done:
     __syncwarp();
     tc_fence_before();
     __syncthreads();
@@ -497,6 +528,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 }
 
 // ------------------------------------------------------------------ host
+
+static int64_t g_pre_min = -1;
+static int64_t pre_min_tokens();
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -536,35 +570,71 @@ static bool map_weights(CUtensorMap *m, const DevWeight &w, int raw_row) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int TYPE, int EPI, bool DOTS>
+// f32 scale (or offset) plane [K/32][rows], box = 128 features x 8 blocks.
+static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t nb) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)rows, (cuuint64_t)nb};
+    cuuint64_t strides[1] = {(cuuint64_t)(rows * 4)};
+    cuuint32_t box[2] = {BN, CHUNK};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)plane, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int TYPE, int EPI, bool DOTS, bool PRE>
 static cudaError_t launch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
     using L = Smem<TYPE>;
-    CUtensorMap ma, mw;
+    CUtensorMap ma, mw, mb, msc, moff;
     if (!map_activations(&ma, q.a16, q.M, w.cols) || !map_weights(&mw, w, L::RAW_ROW)) return cudaErrorInvalidValue;
-    auto kern = k_gemm_tc<TYPE, EPI, DOTS>;
+    mb = msc = moff = ma;  // placeholders the raw path never reads
+    if (PRE) {
+        if (!map_activations(&mb, w.w16, w.rows, w.cols) || !map_plane(&msc, w.scale_plane, w.rows, w.cols / 32))
+            return cudaErrorInvalidValue;
+        if (has_offset(TYPE) && !map_plane(&moff, w.offset_plane, w.rows, w.cols / 32)) return cudaErrorInvalidValue;
+    }
+    auto kern = k_gemm_tc<TYPE, EPI, DOTS, PRE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)((w.rows + BN - 1) / BN), (unsigned)((q.M + BM - 1) / BM));
-    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, q.da, q.ds, y, ldy, (int)q.M, (int)w.rows, (int)(w.cols / 32), err,
-                                         dots);
+    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, mb, msc, moff, q.da, q.ds, y, ldy, (int)q.M, (int)w.rows,
+                                         (int)(w.cols / 32), err, dots);
     return cudaGetLastError();
 }
 
-template <int EPI, bool DOTS>
-static cudaError_t dispatch(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
-                            cudaStream_t s) {
+template <int EPI, bool DOTS, bool PRE>
+static cudaError_t dispatch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+                              cudaStream_t s) {
     switch (w.type) {
-    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
-    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS>(w, q, y, ldy, err, dots, s);
-    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
-    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS>(w, q, y, ldy, err, dots, s);
-    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS>(w, q, y, ldy, err, dots, s);
+    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
+    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
+    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
+    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
+    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
     default: return cudaErrorNotSupported;
     }
 }
 
+// Long token batches read the pre-unpacked copy (every 128-token tile would
+// otherwise unpack the same weights again); short ones stream the raw blocks.
+constexpr int64_t PRE_MIN_TOKENS = 256;
+static int64_t pre_min_tokens() { return g_pre_min >= 0 ? g_pre_min : PRE_MIN_TOKENS; }
+
+template <int EPI, bool DOTS>
+static cudaError_t dispatch(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+                            cudaStream_t s) {
+    if (w.w16 && w.scale_plane && (!has_offset(w.type) || w.offset_plane) && q.M >= pre_min_tokens())
+        return dispatch_t<EPI, DOTS, true>(w, q, y, ldy, err, dots, s);
+    return dispatch_t<EPI, DOTS, false>(w, q, y, ldy, err, dots, s);
+}
+
 }  // namespace tc
+
+// Token count from which the tensor-core GEMM reads the pre-unpacked weights
+// (negative: the built-in default). Used by tests to cover both paths.
+void gemm_tc_set_pre_min_tokens(int64_t m) { tc::g_pre_min = m; }
 
 bool gemm_tc_supports(const DevWeight &w, int64_t M) {
     if (!block_bytes(w.type) || w.cols % 256 || w.rows % 16 || M < 1 || M > (1LL << 31) - 1) return false;

@@ -40,6 +40,9 @@ struct DevWeight {
     const uint8_t *data = nullptr;
     float *scale_plane = nullptr;
     float *offset_plane = nullptr;
+    // the weights unpacked once to f16 integers (u - z), row-major [rows][cols],
+    // for the tensor-core GEMM on long token batches (null when not built)
+    __half *w16 = nullptr;
 };
 
 enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1 };
@@ -52,6 +55,7 @@ cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t
 cudaError_t launch_embed(const DevWeight &emb, const int32_t *ids, int64_t M, float *h, int32_t *err,
                          cudaStream_t s);
 cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s);
+cudaError_t launch_unpack_f16(const DevWeight &w, cudaStream_t s);
 
 // Exact integer GEMM on CUDA cores; any K % 32 == 0, optional row subset.
 cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
@@ -61,6 +65,7 @@ cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t
 cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
                            cudaStream_t s);
 bool gemm_tc_supports(const DevWeight &w, int64_t M);
+void gemm_tc_set_pre_min_tokens(int64_t m);
 // Per-block int32 dots (t, n, b) for the bit-exactness check.
 cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s);
 cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s);

@@ -169,4 +169,35 @@ cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// One thread per (row, block): the block's 32 weights as f16 integers w = u - z
+// (Q4_1/Q5_1: u), exact in f16, in weight order.
+template <int TYPE>
+__global__ void k_unpack_f16(const uint8_t *__restrict__ data, int64_t rows, int64_t row_bytes, int64_t nb,
+                             __half *__restrict__ out) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * nb) return;
+    int64_t r = i / nb, b = i % nb;
+    const uint8_t *blk = data + r * row_bytes + b * block_bytes(TYPE);
+    __half *dst = out + r * nb * 32 + b * 32;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2)
+        *reinterpret_cast<__half2 *>(dst + j) =
+            __halves2half2(__int2half_rn(weight_at<TYPE>(blk, j)), __int2half_rn(weight_at<TYPE>(blk, j + 1)));
+}
+
+cudaError_t launch_unpack_f16(const DevWeight &w, cudaStream_t s) {
+    int64_t n = w.rows * (w.cols / 32);
+    if (!w.w16 || n == 0) return cudaSuccess;
+    unsigned g = (unsigned)((n + 255) / 256);
+    switch (w.type) {
+    case T_Q4_0: k_unpack_f16<T_Q4_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, w.w16); break;
+    case T_Q4_1: k_unpack_f16<T_Q4_1><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, w.w16); break;
+    case T_Q5_0: k_unpack_f16<T_Q5_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, w.w16); break;
+    case T_Q5_1: k_unpack_f16<T_Q5_1><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, w.w16); break;
+    case T_Q8_0: k_unpack_f16<T_Q8_0><<<g, 256, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols / 32, w.w16); break;
+    default: return cudaErrorNotSupported;
+    }
+    return cudaGetLastError();
+}
+
 }  // namespace shield

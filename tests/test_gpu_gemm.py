@@ -27,7 +27,11 @@ def upload(ctx, name, qtype, rows, cols, w):
     ctx.upload(name, qtype, rows, cols, w)
 
 
-@pytest.mark.parametrize("path", [1, 2])
+# 1: CUDA cores; 2: tensor cores unpacking GGUF blocks; 3: tensor cores on the f16 copy
+PATHS = [1, 2, 3]
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("qtype", INT_TYPES)
 def test_block_dots_bit_exact(ctx, qtype, path):
     """Per-block int32 dot products equal the oracle's i = -z·Σa + Σ u·a."""
@@ -36,16 +40,15 @@ def test_block_dots_bit_exact(ctx, qtype, path):
     x = np.random.default_rng(qtype).standard_normal((tokens, cols)).astype(np.float32) * 3
     upload(ctx, "blk.0.attn_q.weight", qtype, rows, cols, w)
     expect = oracle.block_dots(qtype, w, rows, cols, x, tokens)
+    ctx.set_gemm_path(path)
     try:
-        got = ctx.block_dots("blk.0.attn_q.weight", x, tokens, rows, cols, path=path)
-    except binding.ShieldError as e:
-        if path == 2 and e.code == binding.ERR_UNSUPPORTED:
-            pytest.skip("tensor-core path not built for this shape")
-        raise
+        got = ctx.block_dots("blk.0.attn_q.weight", x, tokens, rows, cols, path=min(path, 2))
+    finally:
+        ctx.set_gemm_path(0)
     np.testing.assert_array_equal(got, expect)
 
 
-@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("qtype", INT_TYPES)
 @pytest.mark.parametrize("rows,cols,tokens", [(100, 256, 13), (256, 768, 130), (128, 3072, 64)])
 def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
@@ -57,7 +60,7 @@ def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
     try:
         got = ctx.qmatmul("blk.0.attn_k.weight", x, tokens, rows)
     except binding.ShieldError as e:
-        if path == 2 and e.code == binding.ERR_UNSUPPORTED:
+        if path >= 2 and e.code == binding.ERR_UNSUPPORTED:
             pytest.skip("tensor-core path does not take this shape")
         raise
     finally:
@@ -69,13 +72,14 @@ def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
 @pytest.mark.parametrize("rows,cols", SWEEP_SHAPES)
 def test_sweep_shapes_match_oracle(ctx, qtype, rows, cols):
     """The isolated-GEMM sweep's shapes on the synthetic N(0, 0.02) weights at
-    M = 64 (plus a single token), bit-identical to the oracle."""
+    M = 1, 64 and 300 (the last above the unpacked-copy threshold),
+    bit-identical to the oracle."""
     w = synth.tensor(qtype, rows, cols, seed=77, stream=rows * 7 + cols)
     upload(ctx, "blk.0.ffn_gate.weight", qtype, rows, cols, w)
-    for M in (1, 64):
+    for M in (1, 64, 300):
         x = np.random.default_rng(M).standard_normal((M, cols)).astype(np.float32)
         np.testing.assert_array_equal(ctx.qmatmul("blk.0.ffn_gate.weight", x, M, rows),
-                                      oracle.qmatmul(qtype, w, rows, cols, x, M))
+                                      oracle.qmatmul(qtype, w, rows, cols, x, M, threads=None))
 
 
 @pytest.mark.parametrize("qtype", INT_TYPES)
