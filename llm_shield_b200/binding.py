@@ -141,7 +141,7 @@ class ShieldContext:
         h = getattr(self, "_h", None)
         if h and _lib is not None:
             _lib.shield_close(h)
-        self._h = C.c_void_p()
+        self._h = None  # module globals may already be gone at interpreter exit
 
     def __del__(self):
         self.close()

@@ -17,8 +17,13 @@
 //   warps 2-3   unpack raw blocks in registers (nibbles, 5th bits, Q8 bytes) to
 //               f16 integers in the canonical SW128 K-major layout; widen the
 //               f16 block scales (and offsets) to f32
-//   warps 4-11  epilogue: tcgen05.ld the slot, apply the block's f32 scaling
-//               chain per output (packed f32x2 operations), write or add to y
+//   warps 4-19  epilogue, 32 output features each: tcgen05.ld the slot, apply
+//               the block's f32 scaling chain per output (packed f32x2
+//               operations), write or add to y
+//
+// The activation scales reach shared memory by TMA beside the weight scales.
+// The grid is persistent (one CTA per SM walking tiles), so a tile's pipeline
+// fill and its final stores hide under its neighbours' work.
 //
 // kind::f16 rather than kind::i8: products of 8-bit integers summed over one
 // block stay below 2^20, so the f32 accumulator holds the exact int32 sum and
@@ -40,7 +45,7 @@ constexpr int RAW_STAGES = 2;    // raw weight chunks in flight
 constexpr int SC_STAGES = 2;     // f32 scale chunks in flight
 constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns)
 constexpr int CHUNK = 8;         // blocks per raw chunk (TMA inner box = 8 blocks)
-constexpr int EPI_WARPS = 8;              // warp e owns lane quarter e%4 and columns EPI_COLS*(e/4)..
+constexpr int EPI_WARPS = 16;              // warp e owns lane quarter e%4 and columns EPI_COLS*(e/4)..
 constexpr int EPI_COLS = BN / (EPI_WARPS / 4);
 constexpr int THREADS = 128 + 32 * EPI_WARPS;
 constexpr int UNPACK_THREADS = 64;
@@ -54,7 +59,11 @@ struct Smem {
     static constexpr int RAW_BYTES = BN * RAW_ROW;
     static constexpr int A_BYTES = BM * 128;     // 64 f16 per row
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int SC_FLOATS = CHUNK * BN * (has_offset(TYPE) ? 2 : 1);
+    // one scale stage: weight scales [CHUNK][BN] (+ offsets), then the
+    // activation scales [BM][CHUNK] (+ their offset terms)
+    static constexpr int SC_DA = CHUNK * BN * (has_offset(TYPE) ? 2 : 1);
+    static constexpr int DA_BYTES = CHUNK * BM * 4 * (has_offset(TYPE) ? 2 : 1);
+    static constexpr int SC_FLOATS = SC_DA + DA_BYTES / 4;
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
@@ -146,31 +155,21 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive TMEM columns of this warp's 32 lanes; the wait names the
+// registers so that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
 }
 
 // Two independent IEEE f32 operations per instruction (sm_100 packed f32x2):
@@ -244,19 +243,25 @@ __device__ __forceinline__ void unpack_block(const uint8_t *blk, uint32_t (&o)[1
 
 // PRE: the weights come pre-unpacked (f16 copy) and their scales from the f32
 // planes, both by TMA; the unpacker warps then idle.
+//
+// Persistent: CTA b takes tiles b, b + gridDim.x, ... (token tiles outer,
+// feature tiles inner) and every ring (operand stages, scale stages, TMEM
+// slots) runs on across tiles, so the next tile's loads and MMAs overlap the
+// current tile's epilogue and final stores.
 template <int TYPE, int EPI, bool DOTS, bool PRE>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
           const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_sc,
-          const __grid_constant__ CUtensorMap map_off,
-          const float *__restrict__ da, const float *__restrict__ ds, float *__restrict__ y, int64_t ldy, int M, int N,
-          int nb, int32_t *__restrict__ err, int32_t *__restrict__ dots) {
+          const __grid_constant__ CUtensorMap map_off, const __grid_constant__ CUtensorMap map_da,
+          const __grid_constant__ CUtensorMap map_ds, float *__restrict__ y, int64_t ldy, int M, int N, int nb,
+          int32_t *__restrict__ err, int32_t *__restrict__ dots) {
     using L = Smem<TYPE>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int ntn = (N + BN - 1) / BN;
+    const int64_t ntiles = (int64_t)ntn * ((M + BM - 1) / BM);
 
     uint32_t bar = sbase + L::OFF_BAR;
     auto a_full = [&](int s) { return bar + 8 * s; };
@@ -285,7 +290,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             mbar_init(raw_empty(s), UNPACK_THREADS);
         }
         for (int s = 0; s < SC_STAGES; s++) {
-            mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS);
+            // filled by TMA (PRE), or by the unpackers plus the producer's
+            // TMA of the activation scales
+            mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS + (DOTS ? 0 : 1));
             mbar_init(sc_empty(s), EPI_WARPS);
         }
         for (int s = 0; s < NSLOT; s++) {
@@ -309,211 +316,251 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
-            for (int p = 0; p < npairs; p++) {
-                if ((2 * p) % CHUNK == 0) {
-                    int c = (2 * p) / CHUNK;
-                    if (PRE) {
-                        int ss = c % SC_STAGES;
-                        if (!mbar_wait(sc_empty(ss), ((c / SC_STAGES) & 1) ^ 1, abort_flag, err)) break;
-                        mbar_expect_tx(sc_full(ss), L::SC_FLOATS * 4);
-                        uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
-                        tma_load_2d(dst, &map_sc, n0, c * CHUNK, sc_full(ss));
-                        if (has_offset(TYPE)) tma_load_2d(dst + CHUNK * BN * 4, &map_off, n0, c * CHUNK, sc_full(ss));
-                    } else {
-                        int rs = c % RAW_STAGES;
-                        if (!mbar_wait(raw_empty(rs), ((c / RAW_STAGES) & 1) ^ 1, abort_flag, err)) break;
-                        mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
-                        tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w,
-                                    c * (L::RAW_ROW / 2), n0, raw_full(rs));
+            uint32_t pc = 0, cc = 0;  // pairs and chunks issued, over all tiles
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
+                for (int p = 0; p < npairs; p++, pc++) {
+                    if ((2 * p) % CHUNK == 0) {
+                        const int c = (2 * p) / CHUNK;
+                        if (!PRE) {
+                            const int rs = cc % RAW_STAGES;
+                            if (!mbar_wait(raw_empty(rs), ((cc / RAW_STAGES) & 1) ^ 1, abort_flag, err)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
+                            tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w,
+                                        c * (L::RAW_ROW / 2), n0, raw_full(rs));
+                        }
+                        if (PRE || !DOTS) {
+                            const int ss = cc % SC_STAGES;
+                            if (!mbar_wait(sc_empty(ss), ((cc / SC_STAGES) & 1) ^ 1, abort_flag, err)) {
+                                ok = false;
+                                break;
+                            }
+                            const uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
+                            mbar_expect_tx(sc_full(ss), (PRE ? L::SC_DA * 4 : 0) + (DOTS ? 0 : L::DA_BYTES));
+                            if (PRE) {
+                                tma_load_2d(dst, &map_sc, n0, c * CHUNK, sc_full(ss));
+                                if (has_offset(TYPE))
+                                    tma_load_2d(dst + CHUNK * BN * 4, &map_off, n0, c * CHUNK, sc_full(ss));
+                            }
+                            if (!DOTS) {
+                                tma_load_2d(dst + L::SC_DA * 4, &map_da, c * CHUNK, m0, sc_full(ss));
+                                if (has_offset(TYPE))
+                                    tma_load_2d(dst + L::SC_DA * 4 + CHUNK * BM * 4, &map_ds, c * CHUNK, m0,
+                                                sc_full(ss));
+                            }
+                        }
+                        cc++;
                     }
+                    const int s = pc % STAGES;
+                    if (!mbar_wait(a_empty(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(a_full(s), L::A_BYTES + (PRE ? L::B_BYTES : 0));
+                    tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &map_a, 2 * p * 32, m0, a_full(s));
+                    if (PRE) tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &map_b, 2 * p * 32, n0, a_full(s));
                 }
-                int s = p % STAGES;
-                if (!mbar_wait(a_empty(s), ((p / STAGES) & 1) ^ 1, abort_flag, err)) break;
-                mbar_expect_tx(a_full(s), L::A_BYTES + (PRE ? L::B_BYTES : 0));
-                tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &map_a, 2 * p * 32, m0, a_full(s));
-                if (PRE) tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &map_b, 2 * p * 32, n0, a_full(s));
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            for (int p = 0; p < npairs; p++) {
-                int s = p % STAGES;
-                uint32_t ph = (p / STAGES) & 1;
-                if (!mbar_wait(a_full(s), ph, abort_flag, err)) break;
-                if (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err)) break;
-                tc_fence_after();
-                bool ok = true;
-                for (int jb = 0; jb < 2; jb++) {
-                    int kb = 2 * p + jb, slot = kb % NSLOT;
-                    if (!mbar_wait(t_empty(slot), ((kb / NSLOT) & 1) ^ 1, abort_flag, err)) {
+            uint32_t pc = 0, kbg = 0;  // pairs and blocks consumed, over all tiles
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                for (int p = 0; p < npairs; p++, pc++) {
+                    const int s = pc % STAGES;
+                    const uint32_t ph = (pc / STAGES) & 1;
+                    if (!mbar_wait(a_full(s), ph, abort_flag, err) ||
+                        (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    uint32_t a_addr = sbase + L::OFF_A + s * L::A_BYTES + jb * 64;
-                    uint32_t b_addr = sbase + L::OFF_B + s * L::B_BYTES + jb * 64;
+                    for (int jb = 0; jb < 2; jb++, kbg++) {
+                        const int slot = kbg % NSLOT;
+                        if (!mbar_wait(t_empty(slot), ((kbg / NSLOT) & 1) ^ 1, abort_flag, err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = sbase + L::OFF_A + s * L::A_BYTES + jb * 64;
+                        const uint32_t b_addr = sbase + L::OFF_B + s * L::B_BYTES + jb * 64;
 #pragma unroll
-                    for (int k = 0; k < 2; k++)
-                        umma_f16(tmem_base + slot * BN, umma_desc_sw128(a_addr + 32 * k),
-                                 umma_desc_sw128(b_addr + 32 * k), k);
-                    umma_commit(t_full(slot));
+                        for (int k = 0; k < 2; k++)
+                            umma_f16(tmem_base + slot * BN, umma_desc_sw128(a_addr + 32 * k),
+                                     umma_desc_sw128(b_addr + 32 * k), k);
+                        umma_commit(t_full(slot));
+                    }
+                    if (!ok) break;
+                    umma_commit(a_empty(s));
+                    if (!PRE) umma_commit(b_empty(s));
                 }
-                if (!ok) break;
-                umma_commit(a_empty(s));
-                if (!PRE) umma_commit(b_empty(s));
             }
         }
     } else if (warp < 4) {
         // ------------------------------------------------------ unpackers
         if (PRE) goto done;
         const int ut = threadIdx.x - 64;
-        for (int c = 0; c < nchunks; c++) {
-            int rs = c % RAW_STAGES, ss = c % SC_STAGES;
-            if (!mbar_wait(raw_full(rs), (c / RAW_STAGES) & 1, abort_flag, err)) break;
-            if (!mbar_wait(sc_empty(ss), ((c / SC_STAGES) & 1) ^ 1, abort_flag, err)) break;
-            const uint8_t *raw = smem + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024);
-            float *sc = sc_base + ss * L::SC_FLOATS;
-            bool ok = true;
-            for (int q = 0; q < CHUNK / 2; q++) {
-                int p = c * (CHUNK / 2) + q, s = p % STAGES;
-                if (!mbar_wait(b_empty(s), ((p / STAGES) & 1) ^ 1, abort_flag, err)) {
+        uint32_t pc = 0, cc = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+            for (int c = 0; c < nchunks; c++, cc++) {
+                const int rs = cc % RAW_STAGES, ss = cc % SC_STAGES;
+                if (!mbar_wait(raw_full(rs), (cc / RAW_STAGES) & 1, abort_flag, err) ||
+                    !mbar_wait(sc_empty(ss), ((cc / SC_STAGES) & 1) ^ 1, abort_flag, err)) {
                     ok = false;
                     break;
                 }
-                uint8_t *bst = smem + L::OFF_B + s * L::B_BYTES;
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int r = ut + rr * 64;
-#pragma unroll
-                    for (int jb = 0; jb < 2; jb++) {
-                        const int j = 2 * q + jb;
-                        const uint8_t *blk = raw + r * L::RAW_ROW + j * L::BB;
-                        uint32_t o[16];
-                        unpack_block<TYPE>(blk, o);
-#pragma unroll
-                        for (int cc = 0; cc < 4; cc++) {
-                            int chunk16 = jb * 4 + cc;
-                            uint4 v = make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]);
-                            *reinterpret_cast<uint4 *>(bst + r * 128 + ((chunk16 ^ (r & 7)) << 4)) = v;
-                        }
-                        sc[j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk));
-                        if (has_offset(TYPE)) sc[CHUNK * BN + j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                const uint8_t *raw = smem + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024);
+                float *sc = sc_base + ss * L::SC_FLOATS;
+                for (int pp = 0; pp < CHUNK / 2; pp++, pc++) {
+                    const int s = pc % STAGES;
+                    if (!mbar_wait(b_empty(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
                     }
+                    uint8_t *bst = smem + L::OFF_B + s * L::B_BYTES;
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++) {
+                        const int r = ut + rr * 64;
+#pragma unroll
+                        for (int jb = 0; jb < 2; jb++) {
+                            const int j = 2 * pp + jb;
+                            const uint8_t *blk = raw + r * L::RAW_ROW + j * L::BB;
+                            uint32_t o[16];
+                            unpack_block<TYPE>(blk, o);
+#pragma unroll
+                            for (int cq = 0; cq < 4; cq++) {
+                                const int chunk16 = jb * 4 + cq;
+                                const uint4 v = make_uint4(o[4 * cq], o[4 * cq + 1], o[4 * cq + 2], o[4 * cq + 3]);
+                                *reinterpret_cast<uint4 *>(bst + r * 128 + ((chunk16 ^ (r & 7)) << 4)) = v;
+                            }
+                            sc[j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk));
+                            if (has_offset(TYPE))
+                                sc[CHUNK * BN + j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                        }
+                    }
+                    fence_proxy_async();
+                    mbar_arrive(b_full(s));
                 }
-                fence_proxy_async();
-                mbar_arrive(b_full(s));
+                if (!ok) break;
+                mbar_arrive(raw_empty(rs));
+                mbar_arrive(sc_full(ss));
             }
-            if (!ok) break;
-            mbar_arrive(raw_empty(rs));
-            mbar_arrive(sc_full(ss));
         }
     } else {
         // ------------------------------------------------------ epilogue
-        const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int g = (warp - 4) >> 2;          // column group: columns g*EPI_COLS ..
-        const int t = q * 32 + lane;            // token within the tile
-        const int m = m0 + t;
-        const bool row_ok = m < M;
-        const bool warp_live = m0 + q * 32 < M;
-        uint64_t f[EPI_COLS / 2];  // this thread's outputs as f32 pairs
+        const int q = warp & 3;             // TMEM lane quarter this warp may access
+        const int g = (warp - 4) >> 2;      // column group: columns g*EPI_COLS ..
+        const int t = q * 32 + lane;        // token within the tile
+        uint32_t kbg = 0, cc = 0;           // blocks and chunks consumed, over all tiles
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+            const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
+            const int m = m0 + t;
+            const bool row_ok = m < M;
+            const bool warp_live = m0 + q * 32 < M;
+            uint64_t f[EPI_COLS / 2];  // this thread's outputs as f32 pairs
 #pragma unroll
-        for (int i = 0; i < EPI_COLS / 2; i++) f[i] = 0;
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
-        // this token's activation scales for the current chunk, the next chunk's in flight
-        float da8[CHUNK], ds8[CHUNK];
-#pragma unroll
-        for (int j = 0; j < CHUNK; j++) {
-            da8[j] = row_ok ? da[(int64_t)m * nb + j] : 0.0f;
-            if (has_offset(TYPE)) ds8[j] = row_ok ? ds[(int64_t)m * nb + j] : 0.0f;
-        }
-        for (int c = 0; c < nchunks; c++) {
-            int ss = c % SC_STAGES;
-            float dn8[CHUNK], sn8[CHUNK];
-            const bool more = row_ok && c + 1 < nchunks;
-#pragma unroll
-            for (int j = 0; j < CHUNK; j++) {
-                dn8[j] = more ? da[(int64_t)m * nb + (c + 1) * CHUNK + j] : 0.0f;
-                if (has_offset(TYPE)) sn8[j] = more ? ds[(int64_t)m * nb + (c + 1) * CHUNK + j] : 0.0f;
-            }
-            if (!mbar_wait(sc_full(ss), (c / SC_STAGES) & 1, abort_flag, err)) break;
-            const float *sc = sc_base + ss * L::SC_FLOATS;
-            bool ok = true;
-#pragma unroll 1
-            for (int j = 0; j < CHUNK; j++) {
-                int kb = c * CHUNK + j, slot = kb % NSLOT;
-                if (!mbar_wait(t_full(slot), (kb / NSLOT) & 1, abort_flag, err)) {
+            for (int i = 0; i < EPI_COLS / 2; i++) f[i] = 0;
+            const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
+            for (int c = 0; c < nchunks; c++, cc++) {
+                const int ss = cc % SC_STAGES;
+                if (!__all_sync(0xffffffffu, mbar_wait(sc_full(ss), (cc / SC_STAGES) & 1, abort_flag, err))) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                const uint64_t da2 = pack2(da8[j], da8[j]);
-                const uint64_t ds2 = has_offset(TYPE) ? pack2(ds8[j], ds8[j]) : 0;
+                const float *sc = sc_base + ss * L::SC_FLOATS;
+                float da8[CHUNK], ds8[CHUNK];
+                if (!DOTS) {
+                    const float4 *d4 = reinterpret_cast<const float4 *>(sc + L::SC_DA + t * CHUNK);
+                    const float4 d0 = d4[0], d1 = d4[1];
+                    da8[0] = d0.x, da8[1] = d0.y, da8[2] = d0.z, da8[3] = d0.w;
+                    da8[4] = d1.x, da8[5] = d1.y, da8[6] = d1.z, da8[7] = d1.w;
+                    if (has_offset(TYPE)) {
+                        const float4 *s4 = reinterpret_cast<const float4 *>(sc + L::SC_DA + CHUNK * BM + t * CHUNK);
+                        const float4 e0 = s4[0], e1 = s4[1];
+                        ds8[0] = e0.x, ds8[1] = e0.y, ds8[2] = e0.z, ds8[3] = e0.w;
+                        ds8[4] = e1.x, ds8[5] = e1.y, ds8[6] = e1.z, ds8[7] = e1.w;
+                    }
+                }
 #pragma unroll
-                for (int h = 0; h < EPI_COLS / 32; h++) {
-                    uint32_t r[32];
-                    tmem_ld32(lane_addr + slot * BN + h * 32, r);
-                    if (DOTS) {
-                        if (row_ok) {
+                for (int j = 0; j < CHUNK; j++, kbg++) {
+                    const int kb = c * CHUNK + j, slot = kbg % NSLOT;
+                    if (!__all_sync(0xffffffffu, mbar_wait(t_full(slot), (kbg / NSLOT) & 1, abort_flag, err))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da2 = DOTS ? 0 : pack2(da8[j], da8[j]);
+                    const uint64_t ds2 = (DOTS || !has_offset(TYPE)) ? 0 : pack2(ds8[j], ds8[j]);
 #pragma unroll
-                            for (int i = 0; i < 32; i++) {
-                                int n = n0 + g * EPI_COLS + h * 32 + i;
-                                if (n < N) dots[((int64_t)m * N + n) * nb + kb] = (int32_t)__uint_as_float(r[i]);
+                    for (int h = 0; h < EPI_COLS / 16; h++) {
+                        uint32_t r[16];
+                        tmem_ld16(lane_addr + slot * BN + h * 16, r);
+                        if (DOTS) {
+                            if (row_ok) {
+#pragma unroll
+                                for (int i = 0; i < 16; i++) {
+                                    const int n = n0 + g * EPI_COLS + h * 16 + i;
+                                    if (n < N) dots[((int64_t)m * N + n) * nb + kb] = (int32_t)__uint_as_float(r[i]);
+                                }
                             }
-                        }
-                    } else if (warp_live) {
-                        const float4 *dw4 = reinterpret_cast<const float4 *>(sc + j * BN + g * EPI_COLS + h * 32);
+                        } else if (warp_live) {
+                            const float4 *dw4 = reinterpret_cast<const float4 *>(sc + j * BN + g * EPI_COLS + h * 16);
 #pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const float4 w = dw4[i];
-                            const int p = h * 16 + 2 * i;
-                            f[p] = fma2(pack2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
-                                        mul2(pack2(w.x, w.y), da2), f[p]);
-                            f[p + 1] = fma2(pack2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
-                                            mul2(pack2(w.z, w.w), da2), f[p + 1]);
-                        }
-                        if (has_offset(TYPE)) {
-                            const float4 *mo4 =
-                                reinterpret_cast<const float4 *>(sc + CHUNK * BN + j * BN + g * EPI_COLS + h * 32);
+                            for (int i = 0; i < 4; i++) {
+                                const float4 w = dw4[i];
+                                const int p = h * 8 + 2 * i;
+                                f[p] = fma2(pack2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
+                                            mul2(pack2(w.x, w.y), da2), f[p]);
+                                f[p + 1] = fma2(pack2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
+                                                mul2(pack2(w.z, w.w), da2), f[p + 1]);
+                            }
+                            if (has_offset(TYPE)) {
+                                const float4 *mo4 =
+                                    reinterpret_cast<const float4 *>(sc + CHUNK * BN + j * BN + g * EPI_COLS + h * 16);
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const float4 o = mo4[i];
-                                const int p = h * 16 + 2 * i;
-                                f[p] = fma2(pack2(o.x, o.y), ds2, f[p]);
-                                f[p + 1] = fma2(pack2(o.z, o.w), ds2, f[p + 1]);
+                                for (int i = 0; i < 4; i++) {
+                                    const float4 o = mo4[i];
+                                    const int p = h * 8 + 2 * i;
+                                    f[p] = fma2(pack2(o.x, o.y), ds2, f[p]);
+                                    f[p + 1] = fma2(pack2(o.z, o.w), ds2, f[p + 1]);
+                                }
                             }
                         }
                     }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(t_empty(slot));
                 }
-                tc_fence_before();
+                if (!ok) break;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(t_empty(slot));
+                if (lane == 0) mbar_arrive(sc_empty(ss));
             }
             if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(sc_empty(ss));
+            if (!DOTS && row_ok && !*abort_flag) {
+                float *dst = y + (int64_t)m * ldy + n0 + g * EPI_COLS;
 #pragma unroll
-            for (int j = 0; j < CHUNK; j++) {
-                da8[j] = dn8[j];
-                if (has_offset(TYPE)) ds8[j] = sn8[j];
-            }
-        }
-        if (!DOTS && row_ok && !*abort_flag) {
-            float *dst = y + (int64_t)m * ldy + n0 + g * EPI_COLS;
-#pragma unroll
-            for (int i = 0; i < EPI_COLS; i += 4) {
-                if (n0 + g * EPI_COLS + i >= N) break;
-                float4 v = make_float4(__uint_as_float((uint32_t)f[i / 2]), __uint_as_float((uint32_t)(f[i / 2] >> 32)),
-                                       __uint_as_float((uint32_t)f[i / 2 + 1]),
-                                       __uint_as_float((uint32_t)(f[i / 2 + 1] >> 32)));
-                if (EPI == EPI_ADD) {
-                    float4 o = *reinterpret_cast<float4 *>(dst + i);
-                    v.x = __fadd_rn(o.x, v.x);
-                    v.y = __fadd_rn(o.y, v.y);
-                    v.z = __fadd_rn(o.z, v.z);
-                    v.w = __fadd_rn(o.w, v.w);
+                for (int i = 0; i < EPI_COLS; i += 4) {
+                    if (n0 + g * EPI_COLS + i >= N) break;
+                    float4 v = make_float4(__uint_as_float((uint32_t)f[i / 2]), __uint_as_float((uint32_t)(f[i / 2] >> 32)),
+                                           __uint_as_float((uint32_t)f[i / 2 + 1]),
+                                           __uint_as_float((uint32_t)(f[i / 2 + 1] >> 32)));
+                    if (EPI == EPI_ADD) {
+                        const float4 o = *reinterpret_cast<const float4 *>(dst + i);
+                        v.x = __fadd_rn(o.x, v.x);
+                        v.y = __fadd_rn(o.y, v.y);
+                        v.z = __fadd_rn(o.z, v.z);
+                        v.w = __fadd_rn(o.w, v.w);
+                    }
+                    *reinterpret_cast<float4 *>(dst + i) = v;
                 }
-                *reinterpret_cast<float4 *>(dst + i) = v;
             }
         }
     }
@@ -583,13 +630,43 @@ static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Per-token activation scales, [M][nb] f32 -> box of CHUNK blocks x BM tokens.
+static bool map_token_scales(CUtensorMap *m, const float *d, int64_t M, int64_t nb) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)nb, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(nb * 4)};
+    cuuint32_t box[2] = {CHUNK, BM};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)d, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// SMs of the current device (persistent grid size), cached per device.
+static int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
 template <int TYPE, int EPI, bool DOTS, bool PRE>
 static cudaError_t launch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
     using L = Smem<TYPE>;
-    CUtensorMap ma, mw, mb, msc, moff;
+    CUtensorMap ma, mw, mb, msc, moff, mda, mds;
     if (!map_activations(&ma, q.a16, q.M, w.cols) || !map_weights(&mw, w, L::RAW_ROW)) return cudaErrorInvalidValue;
-    mb = msc = moff = ma;  // placeholders the raw path never reads
+    mb = msc = moff = mda = mds = ma;  // placeholders for the maps a variant never reads
+    if (!DOTS) {
+        if (!map_token_scales(&mda, q.da, q.M, w.cols / 32)) return cudaErrorInvalidValue;
+        if (has_offset(TYPE) && !map_token_scales(&mds, q.ds, q.M, w.cols / 32)) return cudaErrorInvalidValue;
+    }
     if (PRE) {
         if (!map_activations(&mb, w.w16, w.rows, w.cols) || !map_plane(&msc, w.scale_plane, w.rows, w.cols / 32))
             return cudaErrorInvalidValue;
@@ -598,8 +675,9 @@ static cudaError_t launch_t(const DevWeight &w, const QAct &q, float *y, int64_t
     auto kern = k_gemm_tc<TYPE, EPI, DOTS, PRE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((w.rows + BN - 1) / BN), (unsigned)((q.M + BM - 1) / BM));
-    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, mb, msc, moff, q.da, q.ds, y, ldy, (int)q.M, (int)w.rows,
+    const int64_t tiles = ((w.rows + BN - 1) / BN) * ((q.M + BM - 1) / BM);
+    const unsigned grid = (unsigned)std::min<int64_t>(tiles, sm_count());
+    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, mb, msc, moff, mda, mds, y, ldy, (int)q.M, (int)w.rows,
                                          (int)(w.cols / 32), err, dots);
     return cudaGetLastError();
 }
@@ -646,7 +724,8 @@ bool gemm_tc_supports(const DevWeight &w, int64_t M) {
 cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
                            cudaStream_t s) {
     if (!gemm_tc_supports(w, q.M) || !q.a16 || ldy % 4 || reinterpret_cast<uintptr_t>(y) % 16 ||
-        reinterpret_cast<uintptr_t>(q.a16) % 16)
+        reinterpret_cast<uintptr_t>(q.a16) % 16 || reinterpret_cast<uintptr_t>(q.da) % 16 ||
+        (has_offset(w.type) && reinterpret_cast<uintptr_t>(q.ds) % 16))
         return cudaErrorNotSupported;
     if (q.M == 0) return cudaSuccess;
     return epi == EPI_ADD ? tc::dispatch<EPI_ADD, false>(w, q, y, ldy, err, nullptr, s)
