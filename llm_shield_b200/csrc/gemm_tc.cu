@@ -13,7 +13,8 @@
 //               128B-swizzled K-major) and raw GGUF weight chunks (8 blocks per
 //               row, bytes unchanged)
 //   warp 1      TMEM owner + MMA issuer: two tcgen05.mma.kind::f16 (K=16) per
-//               block into one of four 128-column TMEM slots
+//               block into one of four 128-column TMEM slots, one commit per
+//               block pair
 //   warps 2-3   unpack raw blocks in registers (nibbles, 5th bits, Q8 bytes) to
 //               f16 integers in the canonical SW128 K-major layout; widen the
 //               f16 block scales (and offsets) to f32
@@ -69,9 +70,9 @@ struct Smem {
     static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
     static constexpr int OFF_SC = OFF_RAW + RAW_STAGES * align_up(RAW_BYTES, 1024);
     static constexpr int OFF_BAR = OFF_SC + SC_STAGES * SC_FLOATS * 4;
-    // barriers: a_full, a_empty, b_full, b_empty (STAGES each), raw_full, raw_empty,
-    // sc_full, sc_empty, t_full, t_empty
-    static constexpr int NBAR = 4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + 2 * NSLOT;
+    // barriers: a_full, b_full, done (STAGES each), raw_full, raw_empty,
+    // sc_full, sc_empty, t_empty (one per TMEM slot pair)
+    static constexpr int NBAR = 3 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + NSLOT / 2;
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 };
@@ -264,16 +265,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     const int64_t ntiles = (int64_t)ntn * ((M + BM - 1) / BM);
 
     uint32_t bar = sbase + L::OFF_BAR;
+    // done(s): one tcgen05.commit per block pair, after its four MMAs. Its
+    // completion frees operand stage s (producer, unpackers) and publishes the
+    // pair's two TMEM slots (epilogue). Every waiter trails the commit by less
+    // than STAGES pairs, so no phase can complete twice under a waiter.
     auto a_full = [&](int s) { return bar + 8 * s; };
-    auto a_empty = [&](int s) { return bar + 8 * (STAGES + s); };
-    auto b_full = [&](int s) { return bar + 8 * (2 * STAGES + s); };
-    auto b_empty = [&](int s) { return bar + 8 * (3 * STAGES + s); };
-    auto raw_full = [&](int s) { return bar + 8 * (4 * STAGES + s); };
-    auto raw_empty = [&](int s) { return bar + 8 * (4 * STAGES + RAW_STAGES + s); };
-    auto sc_full = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + s); };
-    auto sc_empty = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + SC_STAGES + s); };
-    auto t_full = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + s); };
-    auto t_empty = [&](int s) { return bar + 8 * (4 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + NSLOT + s); };
+    auto b_full = [&](int s) { return bar + 8 * (STAGES + s); };
+    auto done = [&](int s) { return bar + 8 * (2 * STAGES + s); };
+    auto raw_full = [&](int s) { return bar + 8 * (3 * STAGES + s); };
+    auto raw_empty = [&](int s) { return bar + 8 * (3 * STAGES + RAW_STAGES + s); };
+    auto sc_full = [&](int s) { return bar + 8 * (3 * STAGES + 2 * RAW_STAGES + s); };
+    auto sc_empty = [&](int s) { return bar + 8 * (3 * STAGES + 2 * RAW_STAGES + SC_STAGES + s); };
+    auto t_empty = [&](int s) { return bar + 8 * (3 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + s); };
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::OFF_MISC + 4);
     float *sc_base = reinterpret_cast<float *>(smem + L::OFF_SC);
@@ -281,9 +284,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(a_full(s), 1);
-            mbar_init(a_empty(s), 1);
             mbar_init(b_full(s), UNPACK_THREADS);
-            mbar_init(b_empty(s), 1);
+            mbar_init(done(s), 1);
         }
         for (int s = 0; s < RAW_STAGES; s++) {
             mbar_init(raw_full(s), 1);
@@ -295,10 +297,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS + (DOTS ? 0 : 1));
             mbar_init(sc_empty(s), EPI_WARPS);
         }
-        for (int s = 0; s < NSLOT; s++) {
-            mbar_init(t_full(s), 1);
-            mbar_init(t_empty(s), EPI_WARPS);
-        }
+        for (int s = 0; s < NSLOT / 2; s++) mbar_init(t_empty(s), EPI_WARPS);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -356,7 +355,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         cc++;
                     }
                     const int s = pc % STAGES;
-                    if (!mbar_wait(a_empty(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
+                    if (!mbar_wait(done(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
@@ -369,36 +368,32 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t pc = 0, kbg = 0;  // pairs and blocks consumed, over all tiles
+            uint32_t pc = 0;  // block pairs consumed, over all tiles
+            const uint64_t adesc0 = umma_desc_sw128(sbase + L::OFF_A), bdesc0 = umma_desc_sw128(sbase + L::OFF_B);
             bool ok = true;
             for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 for (int p = 0; p < npairs; p++, pc++) {
-                    const int s = pc % STAGES;
+                    const int s = pc % STAGES, ps = pc % (NSLOT / 2);
                     const uint32_t ph = (pc / STAGES) & 1;
                     if (!mbar_wait(a_full(s), ph, abort_flag, err) ||
-                        (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err))) {
+                        (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err)) ||
+                        !mbar_wait(t_empty(ps), ((pc / (NSLOT / 2)) & 1) ^ 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    for (int jb = 0; jb < 2; jb++, kbg++) {
-                        const int slot = kbg % NSLOT;
-                        if (!mbar_wait(t_empty(slot), ((kbg / NSLOT) & 1) ^ 1, abort_flag, err)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t a_addr = sbase + L::OFF_A + s * L::A_BYTES + jb * 64;
-                        const uint32_t b_addr = sbase + L::OFF_B + s * L::B_BYTES + jb * 64;
+                    // descriptors advance in 16-byte units: +jb*64 bytes per
+                    // block, +32 bytes per K=16 step
 #pragma unroll
-                        for (int k = 0; k < 2; k++)
-                            umma_f16(tmem_base + slot * BN, umma_desc_sw128(a_addr + 32 * k),
-                                     umma_desc_sw128(b_addr + 32 * k), k);
-                        umma_commit(t_full(slot));
+                    for (int jb = 0; jb < 2; jb++) {
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const uint32_t off = (uint32_t)(jb * 64 + 32 * k) >> 4;
+                            umma_f16(tmem_base + (2 * ps + jb) * BN, adesc0 + (uint32_t)(s * L::A_BYTES >> 4) + off,
+                                     bdesc0 + (uint32_t)(s * L::B_BYTES >> 4) + off, k);
+                        }
                     }
-                    if (!ok) break;
-                    umma_commit(a_empty(s));
-                    if (!PRE) umma_commit(b_empty(s));
+                    umma_commit(done(s));
                 }
             }
         }
@@ -420,7 +415,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 float *sc = sc_base + ss * L::SC_FLOATS;
                 for (int pp = 0; pp < CHUNK / 2; pp++, pc++) {
                     const int s = pc % STAGES;
-                    if (!mbar_wait(b_empty(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
+                    if (!mbar_wait(done(s), ((pc / STAGES) & 1) ^ 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
@@ -492,11 +487,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 #pragma unroll
                 for (int j = 0; j < CHUNK; j++, kbg++) {
                     const int kb = c * CHUNK + j, slot = kbg % NSLOT;
-                    if (!__all_sync(0xffffffffu, mbar_wait(t_full(slot), (kbg / NSLOT) & 1, abort_flag, err))) {
-                        ok = false;
-                        break;
+                    const uint32_t pcg = kbg / 2;  // block pair, over all tiles
+                    if (j % 2 == 0) {
+                        if (!__all_sync(0xffffffffu, mbar_wait(done(pcg % STAGES), (pcg / STAGES) & 1, abort_flag, err))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
                     }
-                    tc_fence_after();
                     const uint64_t da2 = DOTS ? 0 : pack2(da8[j], da8[j]);
                     const uint64_t ds2 = (DOTS || !has_offset(TYPE)) ? 0 : pack2(ds8[j], ds8[j]);
 #pragma unroll
@@ -535,9 +533,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             }
                         }
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(t_empty(slot));
+                    if (j % 2 == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(t_empty(pcg % (NSLOT / 2)));
+                    }
                 }
                 if (!ok) break;
                 __syncwarp();
