@@ -65,6 +65,8 @@ struct Smem {
     static constexpr int SC_DA = CHUNK * BN * (has_offset(TYPE) ? 2 : 1);
     static constexpr int DA_BYTES = CHUNK * BM * 4 * (has_offset(TYPE) ? 2 : 1);
     static constexpr int SC_FLOATS = SC_DA + DA_BYTES / 4;
+    static_assert((SC_DA * 4) % 256 == 0 && (SC_FLOATS * 4) % 256 == 0, "swizzled TMA tiles need 256-byte alignment");
+    static_assert(EPI_COLS == 32, "the epilogue's TMEM loads cover 32 columns per warp");
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
@@ -156,11 +158,12 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                  : "memory");
 }
 
-// 16 consecutive TMEM columns of this warp's 32 lanes; the wait names the
-// registers so that no use of them is scheduled before it.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// tcgen05.ld 16x256b.x4: 16 TMEM lanes x 32 columns. Register 4i + e holds
+// column 8i + 2(lane%4) + (e&1) of lane lane/4 + 8(e>>1), relative to taddr.
+// The wait names the registers so that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
@@ -172,6 +175,11 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                  :
                  : "memory");
 }
+
+// Word of token T's scale for block j in a [BM][CHUNK] f32 tile stored by TMA
+// with 32-byte swizzling (the 16-byte halves of a 32-byte row swap when bit 2
+// of the row is set), which spreads 8 consecutive tokens over all banks.
+__device__ __forceinline__ int da_word(int T, int j) { return T * CHUNK + (j ^ (((T >> 2) & 1) << 2)); }
 
 // Two independent IEEE f32 operations per instruction (sm_100 packed f32x2):
 // each lane rounds exactly as the scalar __fmul_rn / __fmaf_rn would.
@@ -450,20 +458,23 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         }
     } else {
         // ------------------------------------------------------ epilogue
-        const int q = warp & 3;             // TMEM lane quarter this warp may access
-        const int g = (warp - 4) >> 2;      // column group: columns g*EPI_COLS ..
-        const int t = q * 32 + lane;        // token within the tile
-        uint32_t kbg = 0, cc = 0;           // blocks and chunks consumed, over all tiles
+        // Warp (q, g) covers TMEM lane quarter q = warp % 4 (tokens 32q ..
+        // 32q+31) and columns 32g .. 32g+31. A tcgen05.ld of shape 16x256b gives
+        // each thread, per 8 columns, 2 adjacent columns (2(lane%4) + {0,1}) of
+        // 2 tokens (lane/4 and lane/4 + 8 of a 16-lane half); two loads cover
+        // the quarter. A thread so owns 4 tokens x 8 columns and reads each
+        // weight scale once for 4 tokens and each token scale once for 8 columns.
+        const int q = warp & 3;
+        const int g = (warp - 4) >> 2;
+        const int tr = lane >> 2, tcol = g * EPI_COLS + (lane & 3) * 2;
+        uint32_t kbg = 0, cc = 0;  // blocks and chunks consumed, over all tiles
         bool ok = true;
         for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
-            const int m = m0 + t;
-            const bool row_ok = m < M;
             const bool warp_live = m0 + q * 32 < M;
-            uint64_t f[EPI_COLS / 2];  // this thread's outputs as f32 pairs
+            uint64_t f[16];  // [token k][column pair i] as f32 pairs
 #pragma unroll
-            for (int i = 0; i < EPI_COLS / 2; i++) f[i] = 0;
-            const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
+            for (int i = 0; i < 16; i++) f[i] = 0;
             for (int c = 0; c < nchunks; c++, cc++) {
                 const int ss = cc % SC_STAGES;
                 if (!__all_sync(0xffffffffu, mbar_wait(sc_full(ss), (cc / SC_STAGES) & 1, abort_flag, err))) {
@@ -471,64 +482,67 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     break;
                 }
                 const float *sc = sc_base + ss * L::SC_FLOATS;
-                float da8[CHUNK], ds8[CHUNK];
-                if (!DOTS) {
-                    const float4 *d4 = reinterpret_cast<const float4 *>(sc + L::SC_DA + t * CHUNK);
-                    const float4 d0 = d4[0], d1 = d4[1];
-                    da8[0] = d0.x, da8[1] = d0.y, da8[2] = d0.z, da8[3] = d0.w;
-                    da8[4] = d1.x, da8[5] = d1.y, da8[6] = d1.z, da8[7] = d1.w;
-                    if (has_offset(TYPE)) {
-                        const float4 *s4 = reinterpret_cast<const float4 *>(sc + L::SC_DA + CHUNK * BM + t * CHUNK);
-                        const float4 e0 = s4[0], e1 = s4[1];
-                        ds8[0] = e0.x, ds8[1] = e0.y, ds8[2] = e0.z, ds8[3] = e0.w;
-                        ds8[4] = e1.x, ds8[5] = e1.y, ds8[6] = e1.z, ds8[7] = e1.w;
-                    }
-                }
 #pragma unroll
                 for (int j = 0; j < CHUNK; j++, kbg++) {
                     const int kb = c * CHUNK + j, slot = kbg % NSLOT;
                     const uint32_t pcg = kbg / 2;  // block pair, over all tiles
                     if (j % 2 == 0) {
-                        if (!__all_sync(0xffffffffu, mbar_wait(done(pcg % STAGES), (pcg / STAGES) & 1, abort_flag, err))) {
+                        if (!__all_sync(0xffffffffu,
+                                        mbar_wait(done(pcg % STAGES), (pcg / STAGES) & 1, abort_flag, err))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                     }
-                    const uint64_t da2 = DOTS ? 0 : pack2(da8[j], da8[j]);
-                    const uint64_t ds2 = (DOTS || !has_offset(TYPE)) ? 0 : pack2(ds8[j], ds8[j]);
+                    uint64_t w2[4], o2[4];
+                    float dav[4], dsv[4];
+                    if (!DOTS && warp_live) {
 #pragma unroll
-                    for (int h = 0; h < EPI_COLS / 16; h++) {
+                        for (int i = 0; i < 4; i++) {
+                            w2[i] = *reinterpret_cast<const uint64_t *>(sc + j * BN + tcol + 8 * i);
+                            if (has_offset(TYPE))
+                                o2[i] = *reinterpret_cast<const uint64_t *>(sc + CHUNK * BN + j * BN + tcol + 8 * i);
+                        }
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const int tk = q * 32 + tr + 8 * k;
+                            dav[k] = sc[L::SC_DA + da_word(tk, j)];
+                            if (has_offset(TYPE)) dsv[k] = sc[L::SC_DA + CHUNK * BM + da_word(tk, j)];
+                        }
+                    }
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
                         uint32_t r[16];
-                        tmem_ld16(lane_addr + slot * BN + h * 16, r);
+                        tmem_ld16x256(tmem_base + ((uint32_t)(q * 32 + 16 * hh) << 16) + slot * BN + g * EPI_COLS, r);
                         if (DOTS) {
-                            if (row_ok) {
 #pragma unroll
-                                for (int i = 0; i < 16; i++) {
-                                    const int n = n0 + g * EPI_COLS + h * 16 + i;
-                                    if (n < N) dots[((int64_t)m * N + n) * nb + kb] = (int32_t)__uint_as_float(r[i]);
-                                }
+                            for (int kk = 0; kk < 2; kk++) {
+                                const int m = m0 + q * 32 + tr + 8 * (2 * hh + kk);
+                                if (m >= M) continue;
+#pragma unroll
+                                for (int i = 0; i < 4; i++)
+#pragma unroll
+                                    for (int e = 0; e < 2; e++) {
+                                        const int n = n0 + tcol + 8 * i + e;
+                                        if (n < N)
+                                            dots[((int64_t)m * N + n) * nb + kb] =
+                                                (int32_t)__uint_as_float(r[4 * i + 2 * kk + e]);
+                                    }
                             }
                         } else if (warp_live) {
-                            const float4 *dw4 = reinterpret_cast<const float4 *>(sc + j * BN + g * EPI_COLS + h * 16);
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const float4 w = dw4[i];
-                                const int p = h * 8 + 2 * i;
-                                f[p] = fma2(pack2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])),
-                                            mul2(pack2(w.x, w.y), da2), f[p]);
-                                f[p + 1] = fma2(pack2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])),
-                                                mul2(pack2(w.z, w.w), da2), f[p + 1]);
-                            }
-                            if (has_offset(TYPE)) {
-                                const float4 *mo4 =
-                                    reinterpret_cast<const float4 *>(sc + CHUNK * BN + j * BN + g * EPI_COLS + h * 16);
+                            for (int kk = 0; kk < 2; kk++) {
+                                const int k = 2 * hh + kk;
+                                const uint64_t da2 = pack2(dav[k], dav[k]);
 #pragma unroll
-                                for (int i = 0; i < 4; i++) {
-                                    const float4 o = mo4[i];
-                                    const int p = h * 8 + 2 * i;
-                                    f[p] = fma2(pack2(o.x, o.y), ds2, f[p]);
-                                    f[p + 1] = fma2(pack2(o.z, o.w), ds2, f[p + 1]);
+                                for (int i = 0; i < 4; i++)
+                                    f[4 * k + i] = fma2(pack2(__uint_as_float(r[4 * i + 2 * kk]),
+                                                              __uint_as_float(r[4 * i + 2 * kk + 1])),
+                                                        mul2(w2[i], da2), f[4 * k + i]);
+                                if (has_offset(TYPE)) {
+                                    const uint64_t ds2 = pack2(dsv[k], dsv[k]);
+#pragma unroll
+                                    for (int i = 0; i < 4; i++) f[4 * k + i] = fma2(o2[i], ds2, f[4 * k + i]);
                                 }
                             }
                         }
@@ -544,22 +558,24 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (lane == 0) mbar_arrive(sc_empty(ss));
             }
             if (!ok) break;
-            if (!DOTS && row_ok && !*abort_flag) {
-                float *dst = y + (int64_t)m * ldy + n0 + g * EPI_COLS;
+            if (!DOTS && !*abort_flag) {
 #pragma unroll
-                for (int i = 0; i < EPI_COLS; i += 4) {
-                    if (n0 + g * EPI_COLS + i >= N) break;
-                    float4 v = make_float4(__uint_as_float((uint32_t)f[i / 2]), __uint_as_float((uint32_t)(f[i / 2] >> 32)),
-                                           __uint_as_float((uint32_t)f[i / 2 + 1]),
-                                           __uint_as_float((uint32_t)(f[i / 2 + 1] >> 32)));
-                    if (EPI == EPI_ADD) {
-                        const float4 o = *reinterpret_cast<const float4 *>(dst + i);
-                        v.x = __fadd_rn(o.x, v.x);
-                        v.y = __fadd_rn(o.y, v.y);
-                        v.z = __fadd_rn(o.z, v.z);
-                        v.w = __fadd_rn(o.w, v.w);
+                for (int k = 0; k < 4; k++) {
+                    const int m = m0 + q * 32 + tr + 8 * k;
+                    if (m >= M) continue;
+                    float *dst = y + (int64_t)m * ldy + n0 + tcol;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        if (n0 + tcol + 8 * i >= N) break;
+                        float2 v = make_float2(__uint_as_float((uint32_t)f[4 * k + i]),
+                                               __uint_as_float((uint32_t)(f[4 * k + i] >> 32)));
+                        if (EPI == EPI_ADD) {
+                            const float2 o = *reinterpret_cast<const float2 *>(dst + 8 * i);
+                            v.x = __fadd_rn(o.x, v.x);
+                            v.y = __fadd_rn(o.y, v.y);
+                        }
+                        *reinterpret_cast<float2 *>(dst + 8 * i) = v;
                     }
-                    *reinterpret_cast<float4 *>(dst + i) = v;
                 }
             }
         }
@@ -630,7 +646,8 @@ static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Per-token activation scales, [M][nb] f32 -> box of CHUNK blocks x BM tokens.
+// Per-token activation scales, [M][nb] f32 -> box of CHUNK blocks x BM tokens,
+// 32-byte swizzled in shared memory (read back through da_word).
 static bool map_token_scales(CUtensorMap *m, const float *d, int64_t M, int64_t nb) {
     auto fn = encode_fn();
     if (!fn) return false;
@@ -639,7 +656,7 @@ static bool map_token_scales(CUtensorMap *m, const float *d, int64_t M, int64_t 
     cuuint32_t box[2] = {CHUNK, BM};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)d, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
