@@ -160,20 +160,16 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 
 // tcgen05.ld 16x256b.x4: 16 TMEM lanes x 32 columns. Register 4i + e holds
 // column 8i + 2(lane%4) + (e&1) of lane lane/4 + 8(e>>1), relative to taddr.
-// The wait names the registers so that no use of them is scheduled before it.
+// Load and wait are one asm statement, so the registers are defined after it.
 __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15])
-                 :
-                 : "memory");
+        : "r"(taddr)
+        : "memory");
 }
 
 // Word of token T's scale for block j in a [BM][CHUNK] f32 tile stored by TMA
@@ -186,6 +182,13 @@ __device__ __forceinline__ int da_word(int T, int j) { return T * CHUNK + (j ^ (
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
     return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
 }
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ float lo_f(uint64_t p) { return __uint_as_float((uint32_t)p); }
+__device__ __forceinline__ float hi_f(uint64_t p) { return __uint_as_float((uint32_t)(p >> 32)); }
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -195,6 +198,19 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     uint64_t d;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
+}
+
+// Shared-memory loads at 32-bit shared addresses (kept in order with the
+// barrier waits that publish the data).
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint64_t lds_b64(uint32_t a) {
+    uint64_t v;
+    asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(a));
+    return v;
 }
 
 // ------------------------------------------------------------ unpacking
@@ -467,28 +483,38 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         const int q = warp & 3;
         const int g = (warp - 4) >> 2;
         const int tr = lane >> 2, tcol = g * EPI_COLS + (lane & 3) * 2;
-        uint32_t kbg = 0, cc = 0;  // blocks and chunks consumed, over all tiles
+        // byte offsets inside a scale stage: this thread's weight-scale pairs,
+        // and its first token's scale row for blocks 0-3 / 4-7 (the 32-byte
+        // swizzle moves the row's halves by +-16 bytes when bit 2 of tr is set)
+        const uint32_t w_off = (uint32_t)tcol * 4;
+        const uint32_t s16 = ((tr >> 2) & 1) << 4;
+        const uint32_t d_off = L::SC_DA * 4 + (uint32_t)(q * 32 + tr) * (CHUNK * 4);
+        const uint32_t d_lo = d_off + s16, d_hi = d_off - s16;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
+        uint32_t cc = 0;               // chunks consumed, over all tiles
+        uint32_t dstage = 0, dphase = 0;  // next block pair's commit barrier and parity
         bool ok = true;
         for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
             const bool warp_live = m0 + q * 32 < M;
-            uint64_t f[16];  // [token k][column pair i] as f32 pairs
+            float f[32];  // [token k][column 2i + e]
 #pragma unroll
-            for (int i = 0; i < 16; i++) f[i] = 0;
+            for (int i = 0; i < 32; i++) f[i] = 0.0f;
             for (int c = 0; c < nchunks; c++, cc++) {
                 const int ss = cc % SC_STAGES;
                 if (!__all_sync(0xffffffffu, mbar_wait(sc_full(ss), (cc / SC_STAGES) & 1, abort_flag, err))) {
                     ok = false;
                     break;
                 }
-                const float *sc = sc_base + ss * L::SC_FLOATS;
+                const uint32_t sc_s = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
+                const uint32_t w_s = sc_s + w_off, dlo_s = sc_s + d_lo, dhi_s = sc_s + d_hi;
 #pragma unroll
-                for (int j = 0; j < CHUNK; j++, kbg++) {
-                    const int kb = c * CHUNK + j, slot = kbg % NSLOT;
-                    const uint32_t pcg = kbg / 2;  // block pair, over all tiles
+                for (int j = 0; j < CHUNK; j++) {
+                    const int kb = c * CHUNK + j, slot = j % NSLOT;  // chunks start on slot 0
                     if (j % 2 == 0) {
-                        if (!__all_sync(0xffffffffu,
-                                        mbar_wait(done(pcg % STAGES), (pcg / STAGES) & 1, abort_flag, err))) {
+                        const bool got = mbar_wait(done(dstage), dphase, abort_flag, err);
+                        if (++dstage == STAGES) dstage = 0, dphase ^= 1;
+                        if (!__all_sync(0xffffffffu, got)) {
                             ok = false;
                             break;
                         }
@@ -499,21 +525,20 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     if (!DOTS && warp_live) {
 #pragma unroll
                         for (int i = 0; i < 4; i++) {
-                            w2[i] = *reinterpret_cast<const uint64_t *>(sc + j * BN + tcol + 8 * i);
-                            if (has_offset(TYPE))
-                                o2[i] = *reinterpret_cast<const uint64_t *>(sc + CHUNK * BN + j * BN + tcol + 8 * i);
+                            w2[i] = lds_b64(w_s + j * BN * 4 + 32 * i);
+                            if (has_offset(TYPE)) o2[i] = lds_b64(w_s + (CHUNK + j) * BN * 4 + 32 * i);
                         }
+                        const uint32_t d_s = (j < 4 ? dlo_s : dhi_s) + 4 * j;
 #pragma unroll
                         for (int k = 0; k < 4; k++) {
-                            const int tk = q * 32 + tr + 8 * k;
-                            dav[k] = sc[L::SC_DA + da_word(tk, j)];
-                            if (has_offset(TYPE)) dsv[k] = sc[L::SC_DA + CHUNK * BM + da_word(tk, j)];
+                            dav[k] = lds_f32(d_s + k * 8 * CHUNK * 4);
+                            if (has_offset(TYPE)) dsv[k] = lds_f32(d_s + CHUNK * BM * 4 + k * 8 * CHUNK * 4);
                         }
                     }
 #pragma unroll
                     for (int hh = 0; hh < 2; hh++) {
                         uint32_t r[16];
-                        tmem_ld16x256(tmem_base + ((uint32_t)(q * 32 + 16 * hh) << 16) + slot * BN + g * EPI_COLS, r);
+                        tmem_ld16x256(t_lane + ((uint32_t)(16 * hh) << 16) + slot * BN, r);
                         if (DOTS) {
 #pragma unroll
                             for (int kk = 0; kk < 2; kk++) {
@@ -533,16 +558,23 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 #pragma unroll
                             for (int kk = 0; kk < 2; kk++) {
                                 const int k = 2 * hh + kk;
-                                const uint64_t da2 = pack2(dav[k], dav[k]);
+                                const uint64_t da2 = pack2u(__float_as_uint(dav[k]), __float_as_uint(dav[k]));
 #pragma unroll
-                                for (int i = 0; i < 4; i++)
-                                    f[4 * k + i] = fma2(pack2(__uint_as_float(r[4 * i + 2 * kk]),
-                                                              __uint_as_float(r[4 * i + 2 * kk + 1])),
-                                                        mul2(w2[i], da2), f[4 * k + i]);
+                                for (int i = 0; i < 4; i++) {
+                                    // the two scale products as one f32x2 multiply, the
+                                    // accumulations as scalar fma on the loaded words
+                                    const uint64_t p2 = mul2(w2[i], da2);
+                                    float *fk = f + 8 * k + 2 * i;
+                                    fk[0] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk]), lo_f(p2), fk[0]);
+                                    fk[1] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk + 1]), hi_f(p2), fk[1]);
+                                }
                                 if (has_offset(TYPE)) {
-                                    const uint64_t ds2 = pack2(dsv[k], dsv[k]);
 #pragma unroll
-                                    for (int i = 0; i < 4; i++) f[4 * k + i] = fma2(o2[i], ds2, f[4 * k + i]);
+                                    for (int i = 0; i < 4; i++) {
+                                        float *fk = f + 8 * k + 2 * i;
+                                        fk[0] = __fmaf_rn(lo_f(o2[i]), dsv[k], fk[0]);
+                                        fk[1] = __fmaf_rn(hi_f(o2[i]), dsv[k], fk[1]);
+                                    }
                                 }
                             }
                         }
@@ -550,7 +582,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     if (j % 2 == 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(t_empty(pcg % (NSLOT / 2)));
+                        if (lane == 0) mbar_arrive(t_empty((j / 2) % (NSLOT / 2)));
                     }
                 }
                 if (!ok) break;
@@ -567,8 +599,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         if (n0 + tcol + 8 * i >= N) break;
-                        float2 v = make_float2(__uint_as_float((uint32_t)f[4 * k + i]),
-                                               __uint_as_float((uint32_t)(f[4 * k + i] >> 32)));
+                        float2 v = make_float2(f[8 * k + 2 * i], f[8 * k + 2 * i + 1]);
                         if (EPI == EPI_ADD) {
                             const float2 o = *reinterpret_cast<const float2 *>(dst + 8 * i);
                             v.x = __fadd_rn(o.x, v.x);
