@@ -73,8 +73,8 @@ struct Smem {
     static constexpr int OFF_SC = OFF_RAW + RAW_STAGES * align_up(RAW_BYTES, 1024);
     static constexpr int OFF_BAR = OFF_SC + SC_STAGES * SC_FLOATS * 4;
     // barriers: a_full, b_full, done (STAGES each), raw_full, raw_empty,
-    // sc_full, sc_empty, t_empty (one per TMEM slot pair)
-    static constexpr int NBAR = 3 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + NSLOT / 2;
+    // sc_full, sc_empty, t_empty (one per TMEM slot)
+    static constexpr int NBAR = 3 * STAGES + 2 * RAW_STAGES + 2 * SC_STAGES + NSLOT;
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 };
@@ -321,7 +321,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS + (DOTS ? 0 : 1));
             mbar_init(sc_empty(s), EPI_WARPS);
         }
-        for (int s = 0; s < NSLOT / 2; s++) mbar_init(t_empty(s), EPI_WARPS);
+        for (int s = 0; s < NSLOT; s++) mbar_init(t_empty(s), EPI_WARPS);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -400,16 +400,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     const int s = pc % STAGES, ps = pc % (NSLOT / 2);
                     const uint32_t ph = (pc / STAGES) & 1;
                     if (!mbar_wait(a_full(s), ph, abort_flag, err) ||
-                        (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err)) ||
-                        !mbar_wait(t_empty(ps), ((pc / (NSLOT / 2)) & 1) ^ 1, abort_flag, err)) {
+                        (!PRE && !mbar_wait(b_full(s), ph, abort_flag, err))) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
                     // descriptors advance in 16-byte units: +jb*64 bytes per
-                    // block, +32 bytes per K=16 step
+                    // block, +32 bytes per K=16 step. Each block's slot is
+                    // waited for on its own, so the first block of a pair can
+                    // start while the epilogue still reads the second's slot.
 #pragma unroll
                     for (int jb = 0; jb < 2; jb++) {
+                        if (!mbar_wait(t_empty(2 * ps + jb), ((pc / (NSLOT / 2)) & 1) ^ 1, abort_flag, err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < 2; k++) {
                             const uint32_t off = (uint32_t)(jb * 64 + 32 * k) >> 4;
@@ -417,6 +422,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                                      bdesc0 + (uint32_t)(s * L::B_BYTES >> 4) + off, k);
                         }
                     }
+                    if (!ok) break;
                     umma_commit(done(s));
                 }
             }
@@ -579,11 +585,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             }
                         }
                     }
-                    if (j % 2 == 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(t_empty((j / 2) % (NSLOT / 2)));
-                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(t_empty(slot));
                 }
                 if (!ok) break;
                 __syncwarp();
