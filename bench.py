@@ -135,6 +135,15 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def gemm_traffic():
+    """DRAM bytes per GEMM launch (read + write), averaged over the GEMM
+    launches of one ncu capture of this command (profiles/)."""
+    p = REPO / "profiles" / "k_gemm_tc_traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get("dram_bytes_per_launch")
+
+
 def cpu_baseline(spec, tensors, ids, offsets, budget_s: float = 20.0):
     """The oracle (C restatement of the reference CPU path) on the host cores,
     on the first requests of the same set, until about budget_s of work."""
@@ -302,7 +311,9 @@ def main():
         "roofline": {"bound": "tensor", "kernel": "quantized GEMM (all projections)",
                      "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
                      "frac": achieved / bf16, "peak_source": f"{src} bf16_tflops (the f16 MMA rate)",
-                     "traffic": None, "gemm_launches_profiled": g["gemm_launches"],
+                     "traffic": gemm_traffic(),
+                     "algorithmic_bytes_per_launch": g["gemm_bytes"] / max(1, g["gemm_launches"]),
+                     "gemm_launches_profiled": g["gemm_launches"],
                      "gemm_share_of_forward": g["gemm_ms"] / g["forward_ms"] if g["forward_ms"] else None},
     }
     line["clocks"] = clocks.summary()
