@@ -481,9 +481,8 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, fn.vec, c.eps, nullptr, qa, s), "ffn norm");
         gemm(C, d, wg, qa, b.g, c.ffn, EPI_STORE);
         gemm(C, d, wu, qa, b.u, c.ffn, EPI_STORE);
-        count_launch(d), check_launch(launch_swiglu(b.g, b.u, M * c.ffn, s), "swiglu");
         QAct qf = qact(b, M, c.ffn);
-        count_launch(d), check_launch(launch_quantize(b.g, M, c.ffn, c.ffn, qf, s), "quantize ffn");
+        count_launch(d), check_launch(launch_swiglu_quantize(b.g, b.u, M, c.ffn, qf, s), "swiglu + quantize");
         gemm(C, d, wd, qf, b.h, c.hidden, EPI_ADD);
         cap(l, SHIELD_ACT_OUTPUT, b.h, c.hidden);
     }

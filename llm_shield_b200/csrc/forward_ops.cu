@@ -272,20 +272,4 @@ cudaError_t launch_attention(const float *q, const float *k, const float *v, flo
 
 int attention_rows_per_cta() { return att::R; }
 
-// Kernels.SwiGlu (Kernels.cs:83-90): u = g*u; g = sigmoid(g)*u, in place in g.
-__global__ void k_swiglu(float *__restrict__ g, float *__restrict__ u, int64_t n) {
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    float gv = g[i];
-    float uv = __fmul_rn(gv, u[i]);
-    float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, shield_expf(-gv)));
-    g[i] = __fmul_rn(sg, uv);
-}
-
-cudaError_t launch_swiglu(float *g, float *u, int64_t n, cudaStream_t s) {
-    if (n == 0) return cudaSuccess;
-    k_swiglu<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(g, u, n);
-    return cudaGetLastError();
-}
-
 }  // namespace shield

@@ -48,6 +48,9 @@ struct DevWeight {
 enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1 };
 
 cudaError_t launch_quantize(const float *x, int64_t M, int64_t K, int64_t ldx, const QAct &q, cudaStream_t s);
+// SwiGLU(g, u) of [M][K] rows (K % 32 == 0) quantized like launch_quantize.
+cudaError_t launch_swiglu_quantize(const float *g, const float *u, int64_t M, int64_t K, const QAct &q,
+                                   cudaStream_t s);
 // RMSNorm (Kernels.cs:26-61) fused with the activation quantizer; rows are
 // optionally gathered (row_idx) and the normalized floats optionally kept (y).
 cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
@@ -87,6 +90,5 @@ cudaError_t launch_attention(const float *q, const float *k, const float *v, flo
                              const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s);
 int attention_rows_per_cta();
-cudaError_t launch_swiglu(float *g, float *u, int64_t n, cudaStream_t s);
 
 }  // namespace shield

@@ -27,12 +27,100 @@ __global__ void k_quantize(const float *__restrict__ x, int64_t M, int64_t K, in
     }
 }
 
+// One thread per 32-block, the block's 32 values in registers: the same
+// operations as k_quantize (max |x|, d = max/127, inv = 1/d or 0,
+// q = rne(x*inv), sum q) without shuffles, the integers stored 16 bytes at a
+// time. With u, the values are first SwiGLU(g = x, u) exactly as k_swiglu
+// computes them (Kernels.cs:83-90), so the f32 product never reaches memory.
+__global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ x, const float *__restrict__ u,
+                                                       int64_t M, int64_t K, int64_t ldx, QAct q) {
+    const int64_t nb = K / 32;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * nb) return;
+    const int64_t t = idx / nb, b = idx % nb;
+    float v[32];
+    const float4 *src = reinterpret_cast<const float4 *>(x + t * ldx + b * 32);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float4 f = __ldg(src + i);
+        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+    }
+    if (u) {
+        const float4 *us = reinterpret_cast<const float4 *>(u + t * ldx + b * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 f = __ldg(us + i);
+            const float uu[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float gv = v[4 * i + e];
+                const float uv = __fmul_rn(gv, uu[e]);
+                const float sg = __frcp_rn(__fadd_rn(1.0f, shield_expf(-gv)));  // == 1/(1+e), correctly rounded
+                v[4 * i + e] = __fmul_rn(sg, uv);
+            }
+        }
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) m = fmaxf(m, fabsf(v[i]));
+    const float d = __fdiv_rn(m, 127.0f);
+    const float inv = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    int qv[32], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        qv[i] = __float2int_rn(__fmul_rn(v[i], inv));
+        sum += qv[i];
+    }
+    const int64_t o = t * K + b * 32;
+    if (q.a8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            w[i] = (uint32_t)(qv[4 * i] & 0xFF) | ((uint32_t)(qv[4 * i + 1] & 0xFF) << 8) |
+                   ((uint32_t)(qv[4 * i + 2] & 0xFF) << 16) | ((uint32_t)(qv[4 * i + 3] & 0xFF) << 24);
+        uint4 *dst = reinterpret_cast<uint4 *>(q.a8 + o);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    if (q.a16) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const __half2 h = __halves2half2(__int2half_rn(qv[2 * i]), __int2half_rn(qv[2 * i + 1]));
+            w[i] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(q.a16 + o);
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
+    const int64_t so = t * nb + b;
+    q.da[so] = d;
+    if (q.ds) q.ds[so] = __fmul_rn(d, (float)sum);
+    if (q.sums) q.sums[so] = sum;
+}
+
+static bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
 cudaError_t launch_quantize(const float *x, int64_t M, int64_t K, int64_t ldx, const QAct &q, cudaStream_t s) {
-    int64_t warps = M * (K / 32);
-    if (warps == 0) return cudaSuccess;
-    int threads = 256;
-    int64_t blocks = (warps * 32 + threads - 1) / threads;
-    k_quantize<<<(unsigned)blocks, threads, 0, s>>>(x, M, K, ldx, q);
+    const int64_t nblk = M * (K / 32);
+    if (nblk == 0) return cudaSuccess;
+    const int threads = 256;
+    if (aligned16(x) && ldx % 4 == 0 && aligned16(q.a8) && aligned16(q.a16)) {
+        k_quantize_rows<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, s>>>(x, nullptr, M, K, ldx, q);
+    } else {
+        const int64_t blocks = (nblk * 32 + threads - 1) / threads;
+        k_quantize<<<(unsigned)blocks, threads, 0, s>>>(x, M, K, ldx, q);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_quantize(const float *g, const float *u, int64_t M, int64_t K, const QAct &q,
+                                   cudaStream_t s) {
+    const int64_t nblk = M * (K / 32);
+    if (nblk == 0) return cudaSuccess;
+    if (!aligned16(g) || !aligned16(u) || K % 32 || !aligned16(q.a8) || !aligned16(q.a16)) return cudaErrorInvalidValue;
+    const int threads = 256;
+    k_quantize_rows<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, s>>>(g, u, M, K, K, q);
     return cudaGetLastError();
 }
 
