@@ -327,7 +327,7 @@ static void ensure_buffers(Ctx &C, Device &d) {
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_meta, (size_t)(4 * T) * 4));
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_logits, (size_t)(T * 64) * 4));
     // attention scores: at least one longest request, at most ~4 GiB beyond that
-    int64_t one = (int64_t)c.n_heads * c.max_positions * c.max_positions;
+    int64_t one = (int64_t)c.n_heads * c.max_positions * score_row_stride(c.max_positions);
     int64_t all = std::min<int64_t>((int64_t)1 << 30, (int64_t)c.n_heads * T * c.max_positions);
     d.buf.scores_cap = std::max(one, all);
     dev_alloc(d.buf.scores, (size_t)d.buf.scores_cap);
@@ -399,7 +399,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         int64_t used = 0;
         AttGroup cur{0, 0};
         for (int r = 0; r < R; r++) {
-            int64_t need = (int64_t)c.n_heads * B.len[r] * B.len[r];
+            int64_t need = (int64_t)c.n_heads * B.len[r] * score_row_stride(B.len[r]);
             if (used + need > b.scores_cap && cur.nw > 0) {
                 groups.push_back(cur);
                 cur = AttGroup{(int)(work.size() / 2), 0};

@@ -59,9 +59,19 @@ constexpr int R = 128;       // query rows per CTA
 constexpr int HD = 128;      // head_dim this kernel is written for
 constexpr int KT = 32;       // keys per tile
 constexpr int LD = HD + 4;   // padded row of a Q/K/V tile in shared memory
-constexpr int LDW = R + 4;   // padded row of a weight tile
 constexpr int THREADS = 256;
+constexpr int PKT = 32;      // keys per PV tile
+constexpr int LDP = PKT + 4; // padded row of a PV weight tile
 }  // namespace att
+
+__device__ __forceinline__ int64_t score_ld(int64_t S) { return score_row_stride(S); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // dim d of a head stored so that FMA chain j (dims j, j+8, ...) is contiguous
 __device__ __forceinline__ int chain_pos(int d) { return (d & 7) * (att::HD / 8) + (d >> 3); }
@@ -141,7 +151,7 @@ k_attn_scores(const float *__restrict__ q, const float *__restrict__ k, float *_
         for (int a = 0; a < 4; a++) {
             const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, pt = q0 + i;
             if (pt >= S) continue;
-            float *dst = scores + base + ((int64_t)(h * G + g) * S + pt) * S;
+            float *dst = scores + base + ((int64_t)(h * G + g) * S + pt) * score_ld(S);
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const int p = kt0 + kl + 8 * b;
@@ -167,7 +177,7 @@ k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const 
         const int i = row / G, g = row % G, pt = q0 + i;
         if (pt >= S) continue;
         const int limit = pt + 1;
-        float *s = scores + base + ((int64_t)(h * G + g) * S + pt) * S;
+        float *s = scores + base + ((int64_t)(h * G + g) * S + pt) * score_ld(S);
         float mx = -INFINITY;
         for (int p = lane; p < limit; p += 32) mx = fmaxf(mx, s[p]);
         mx = warp_max(mx);
@@ -186,60 +196,101 @@ k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const 
     }
 }
 
+// ctx[row][d] = sum over keys p in order of fma(v[p][d], w[row][p], .)
+// (MinistralModel.cs:372-440). Key tiles of V and of the softmax weights are
+// double-buffered in shared memory by cp.async; thread (tr, td) owns rows
+// tr + 32a and dims td*4 + 32e (a, e < 4).
 __global__ void __launch_bounds__(att::THREADS, 2)
 k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *__restrict__ ctx,
           const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
           const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads) {
     using namespace att;
     extern __shared__ float sm[];
-    float *Vs = sm;             // KT x LD
-    float *Ws = sm + KT * LD;   // KT x LDW  (key-major: the 128 rows' weights of one key)
+    constexpr int V_FLOATS = PKT * LD, W_FLOATS = R * LDP;
     const int G = n_heads / n_kv_heads, QT = R / G;
     const int2 wk = work[blockIdx.x];
     const int h = blockIdx.y, r = wk.x, q0 = wk.y;
     const int S = req_len[r];
-    const int64_t start = req_start[r], base = req_base[r];
+    const int64_t start = req_start[r], base = req_base[r], ld = score_ld(S);
     const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
-    const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;  // rows tr*4.., dims td*4 + 32e ..
+    const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;
     const int qend = min(q0 + QT, S);
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
+    auto Vs = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS); };
+    auto Ws = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS) + V_FLOATS; };
+    auto load = [&](int st, int kt0) {
+        const uint32_t vb = sbase + (uint32_t)(st * (V_FLOATS + W_FLOATS)) * 4, wb = vb + V_FLOATS * 4;
+#pragma unroll
+        for (int it = 0; it < PKT * (HD / 4) / THREADS; it++) {
+            const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
+            const bool ok = p < qend;
+            cp_async16(vb + (uint32_t)(kk * LD + c4 * 4) * 4, ok ? v + (start + p) * kvdim + (int64_t)h * HD + c4 * 4 : v, ok);
+        }
+#pragma unroll
+        for (int it = 0; it < R * (PKT / 4) / THREADS; it++) {
+            const int idx = tid + it * THREADS, row = idx / (PKT / 4), c4 = idx % (PKT / 4);
+            const int i = row / G, g = row % G, pt = q0 + i, p = kt0 + c4 * 4;
+            const bool ok = pt < S && p < qend;
+            cp_async16(wb + (uint32_t)(row * LDP + c4 * 4) * 4,
+                       ok ? scores + base + ((int64_t)(h * G + g) * S + pt) * ld + p : scores, ok);
+        }
+    };
     float c[4][16];
 #pragma unroll
     for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int e = 0; e < 16; e++) c[a][e] = 0.0f;
-    for (int kt0 = 0; kt0 < qend; kt0 += KT) {
+    load(0, 0);
+    cp_async_commit();
+    for (int kt0 = 0, st = 0; kt0 < qend; kt0 += PKT, st ^= 1) {
+        if (kt0 + PKT < qend) load(st ^ 1, kt0 + PKT);
+        cp_async_commit();
+        cp_async_wait1();
         __syncthreads();
-        for (int idx = tid; idx < KT * HD; idx += THREADS) {
-            int kk = idx / HD, d = idx % HD, p = kt0 + kk;
-            Vs[kk * LD + d] = p < qend ? v[(start + p) * kvdim + (int64_t)h * HD + d] : 0.0f;
-        }
-        for (int idx = tid; idx < R * KT; idx += THREADS) {
-            int row = idx / KT, kk = idx % KT, p = kt0 + kk, i = row / G, g = row % G, pt = q0 + i;
-            float w = 0.0f;
-            if (pt < S && p < qend) w = scores[base + ((int64_t)(h * G + g) * S + pt) * S + p];
-            Ws[kk * LDW + row] = w;
-        }
-        __syncthreads();
-        const int kn = min(KT, qend - kt0);
-        for (int kk = 0; kk < kn; kk++) {
-            const float4 w = *reinterpret_cast<const float4 *>(&Ws[kk * LDW + tr * 4]);
-            const float wr[4] = {w.x, w.y, w.z, w.w};
+        const float *V = Vs(st), *W = Ws(st);
+        const int kn = min(PKT, qend - kt0);
+        int kk = 0;
+        for (; kk + 4 <= kn; kk += 4) {
+            float4 w[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float4 vv = *reinterpret_cast<const float4 *>(&Vs[kk * LD + td * 4 + 32 * e]);
+            for (int a = 0; a < 4; a++) w[a] = *reinterpret_cast<const float4 *>(&W[(tr + 32 * a) * LDP + kk]);
 #pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    c[a][4 * e + 0] = __fmaf_rn(vv.x, wr[a], c[a][4 * e + 0]);
-                    c[a][4 * e + 1] = __fmaf_rn(vv.y, wr[a], c[a][4 * e + 1]);
-                    c[a][4 * e + 2] = __fmaf_rn(vv.z, wr[a], c[a][4 * e + 2]);
-                    c[a][4 * e + 3] = __fmaf_rn(vv.w, wr[a], c[a][4 * e + 3]);
+            for (int j = 0; j < 4; j++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float4 vv = *reinterpret_cast<const float4 *>(&V[(kk + j) * LD + td * 4 + 32 * e]);
+#pragma unroll
+                    for (int a = 0; a < 4; a++) {
+                        const float wa = j == 0 ? w[a].x : j == 1 ? w[a].y : j == 2 ? w[a].z : w[a].w;
+                        c[a][4 * e + 0] = __fmaf_rn(vv.x, wa, c[a][4 * e + 0]);
+                        c[a][4 * e + 1] = __fmaf_rn(vv.y, wa, c[a][4 * e + 1]);
+                        c[a][4 * e + 2] = __fmaf_rn(vv.z, wa, c[a][4 * e + 2]);
+                        c[a][4 * e + 3] = __fmaf_rn(vv.w, wa, c[a][4 * e + 3]);
+                    }
                 }
             }
         }
+        for (; kk < kn; kk++) {
+            float wa[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) wa[a] = W[(tr + 32 * a) * LDP + kk];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float4 vv = *reinterpret_cast<const float4 *>(&V[kk * LD + td * 4 + 32 * e]);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    c[a][4 * e + 0] = __fmaf_rn(vv.x, wa[a], c[a][4 * e + 0]);
+                    c[a][4 * e + 1] = __fmaf_rn(vv.y, wa[a], c[a][4 * e + 1]);
+                    c[a][4 * e + 2] = __fmaf_rn(vv.z, wa[a], c[a][4 * e + 2]);
+                    c[a][4 * e + 3] = __fmaf_rn(vv.w, wa[a], c[a][4 * e + 3]);
+                }
+            }
+        }
+        __syncthreads();
     }
 #pragma unroll
     for (int a = 0; a < 4; a++) {
-        const int row = tr * 4 + a, i = row / G, g = row % G, pt = q0 + i;
+        const int row = tr + 32 * a, i = row / G, g = row % G, pt = q0 + i;
         if (pt >= S) continue;
         float *dst = ctx + (start + pt) * qdim + (int64_t)(h * G + g) * HD;
 #pragma unroll
@@ -256,7 +307,7 @@ cudaError_t launch_attention(const float *q, const float *k, const float *v, flo
     using namespace att;
     if (n_work == 0) return cudaSuccess;
     if (head_dim != HD || n_heads % n_kv_heads || R % (n_heads / n_kv_heads)) return cudaErrorInvalidValue;
-    const size_t smem_s = (size_t)(R + KT) * LD * 4, smem_pv = (size_t)KT * (LD + LDW) * 4;
+    const size_t smem_s = (size_t)(R + KT) * LD * 4, smem_pv = (size_t)2 * (PKT * LD + R * LDP) * 4;
     cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)n_work, (unsigned)n_kv_heads);
@@ -265,6 +316,8 @@ cudaError_t launch_attention(const float *q, const float *k, const float *v, flo
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_attn_softmax<<<grid, THREADS, 0, s>>>(scores, work, req_len, req_base, n_heads, n_kv_heads);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pv);
+    if (e != cudaSuccess) return e;
     k_attn_pv<<<grid, THREADS, smem_pv, s>>>(v, scores, ctx, work, req_start, req_len, req_base, n_heads,
                                              n_kv_heads);
     return cudaGetLastError();

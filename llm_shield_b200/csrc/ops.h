@@ -90,5 +90,8 @@ cudaError_t launch_attention(const float *q, const float *k, const float *v, flo
                              const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s);
 int attention_rows_per_cta();
+// Scores of one (head, query) row are stored with a row stride rounded up to
+// 4 floats, so that every row starts on a 16-byte boundary.
+constexpr int64_t score_row_stride(int64_t S) { return (S + 3) & ~int64_t(3); }
 
 }  // namespace shield
