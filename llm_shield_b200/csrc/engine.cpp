@@ -129,6 +129,7 @@ static void dev_free(T *&p) {
 struct Buffers {
     int64_t cap = 0;  // tokens
     float *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ctx = nullptr, *g = nullptr, *u = nullptr;
+    float *kc = nullptr;       // keys after RoPE, chain-major per head (attention's layout)
     int8_t *a8 = nullptr;
     __half *a16 = nullptr;
     float *da = nullptr, *ds = nullptr;
@@ -144,7 +145,7 @@ struct Buffers {
     int32_t *h_meta = nullptr;  // pinned
     float *h_logits = nullptr;  // pinned
     void free_all() {
-        dev_free(h); dev_free(q); dev_free(k); dev_free(v); dev_free(ctx); dev_free(g); dev_free(u);
+        dev_free(h); dev_free(q); dev_free(k); dev_free(kc); dev_free(v); dev_free(ctx); dev_free(g); dev_free(u);
         dev_free(a8); dev_free(a16); dev_free(da); dev_free(ds); dev_free(sums); dev_free(meta);
         dev_free(logits); dev_free(verdict); dev_free(err); dev_free(scores); dev_free(att);
         if (h_att) cudaFreeHost(h_att);
@@ -310,6 +311,7 @@ static void ensure_buffers(Ctx &C, Device &d) {
     dev_alloc(d.buf.h, (size_t)(T * c.hidden));
     dev_alloc(d.buf.q, (size_t)(T * c.qdim()));
     dev_alloc(d.buf.k, (size_t)(T * c.kvdim()));
+    dev_alloc(d.buf.kc, (size_t)(T * c.kvdim()));
     dev_alloc(d.buf.v, (size_t)(T * c.kvdim()));
     dev_alloc(d.buf.ctx, (size_t)(T * c.qdim()));
     dev_alloc(d.buf.g, (size_t)(T * c.ffn));
@@ -460,15 +462,15 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
         gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
         count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 d.temp, s), "rope q");
+                                 d.temp, nullptr, s), "rope q");
         count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 nullptr, s), "rope k");
+                                 nullptr, b.kc, s), "rope k");
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());
         for (const AttGroup &ag : groups) {
             d.timing.launches += 3;
-            check_launch(launch_attention(b.q, b.k, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
+            check_launch(launch_attention(b.q, b.kc, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
                                           d_rbase, c.n_heads, c.n_kv_heads, c.head_dim, scale, s),
                          "attention");
         }

@@ -6,54 +6,6 @@
 
 namespace shield {
 
-// Rope.Apply (Rope.cs:112-135) on adjacent pairs, with cos/sin taken from the
-// per-position table the host computed (cos(pos·freq)·mscale), and the
-// attention temperature of MinistralModel.ApplyPositionScale (:476-482) as a
-// per-position factor (nullptr = none). Products and sums are rounded
-// separately, as the reference writes them.
-__global__ void k_rope(float *__restrict__ x, int64_t M, int heads, int head_dim, int64_t ld,
-                       const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
-                       const float *__restrict__ sin_t, int half, const float *__restrict__ temp) {
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    int64_t per_tok = (int64_t)heads * half;
-    if (i >= M * per_tok) return;
-    int64_t t = i / per_tok;
-    int h = (int)((i % per_tok) / half), p = (int)(i % half);
-    int ps = pos[t];
-    float c = cos_t[(int64_t)ps * half + p], s = sin_t[(int64_t)ps * half + p];
-    float *hd = x + t * ld + (int64_t)h * head_dim;
-    float x0 = hd[2 * p], x1 = hd[2 * p + 1];
-    float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    if (temp) {
-        float f = temp[ps];
-        y0 = __fmul_rn(y0, f);
-        y1 = __fmul_rn(y1, f);
-    }
-    hd[2 * p] = y0;
-    hd[2 * p + 1] = y1;
-}
-
-cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
-                        const float *cos_t, const float *sin_t, int half, const float *temp, cudaStream_t s) {
-    int64_t n = M * heads * half;
-    if (n == 0) return cudaSuccess;
-    k_rope<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, M, heads, head_dim, ld, pos, cos_t, sin_t, half, temp);
-    return cudaGetLastError();
-}
-
-// Causal grouped-query attention over a ragged batch (AttendGroup,
-// MinistralModel.cs:372-440), in three kernels that keep the oracle's exact
-// operation order, so the context is bit-identical to it:
-//   k_attn_scores   s = (Σ over 8 FMA chains, folded as Vector.Sum) * scale,
-//                   chain j = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4)
-//   k_attn_softmax  max, shield_expf(s - max), 32 lane-strided partial sums
-//                   folded pairwise, division (Kernels.Softmax)
-//   k_attn_pv       ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
-// One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
-// the G query heads sharing that KV head, so each key and value row is read
-// once per CTA for all of them. Scores live in a scratch buffer laid out per
-// request as [head][position][key] (S x S per head).
 namespace att {
 constexpr int R = 128;       // query rows per CTA
 constexpr int HD = 128;      // head_dim this kernel is written for
@@ -76,14 +28,72 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 // dim d of a head stored so that FMA chain j (dims j, j+8, ...) is contiguous
 __device__ __forceinline__ int chain_pos(int d) { return (d & 7) * (att::HD / 8) + (d >> 3); }
 
+// Rope.Apply (Rope.cs:112-135) on adjacent pairs, with cos/sin taken from the
+// per-position table the host computed (cos(pos·freq)·mscale), and the
+// attention temperature of MinistralModel.ApplyPositionScale (:476-482) as a
+// per-position factor (nullptr = none). Products and sums are rounded
+// separately, as the reference writes them. With perm, the rotated heads are
+// also written in the attention's chain-major order (see chain_pos).
+__global__ void k_rope(float *__restrict__ x, int64_t M, int heads, int head_dim, int64_t ld,
+                       const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
+                       const float *__restrict__ sin_t, int half, const float *__restrict__ temp,
+                       float *__restrict__ perm) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t per_tok = (int64_t)heads * half;
+    if (i >= M * per_tok) return;
+    int64_t t = i / per_tok;
+    int h = (int)((i % per_tok) / half), p = (int)(i % half);
+    int ps = pos[t];
+    float c = cos_t[(int64_t)ps * half + p], s = sin_t[(int64_t)ps * half + p];
+    float *hd = x + t * ld + (int64_t)h * head_dim;
+    float x0 = hd[2 * p], x1 = hd[2 * p + 1];
+    float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    if (temp) {
+        float f = temp[ps];
+        y0 = __fmul_rn(y0, f);
+        y1 = __fmul_rn(y1, f);
+    }
+    hd[2 * p] = y0;
+    hd[2 * p + 1] = y1;
+    if (perm) {
+        float *ph = perm + t * ld + (int64_t)h * head_dim;
+        ph[chain_pos(2 * p)] = y0;
+        ph[chain_pos(2 * p + 1)] = y1;
+    }
+}
+
+cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
+                        const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
+                        cudaStream_t s) {
+    int64_t n = M * heads * half;
+    if (n == 0) return cudaSuccess;
+    if (perm && head_dim != att::HD) return cudaErrorInvalidValue;
+    k_rope<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, M, heads, head_dim, ld, pos, cos_t, sin_t, half, temp,
+                                                        perm);
+    return cudaGetLastError();
+}
+
+// Causal grouped-query attention over a ragged batch (AttendGroup,
+// MinistralModel.cs:372-440), in three kernels that keep the oracle's exact
+// operation order, so the context is bit-identical to it:
+//   k_attn_scores   s = (Σ over 8 FMA chains, folded as Vector.Sum) * scale,
+//                   chain j = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4)
+//   k_attn_softmax  max, shield_expf(s - max), 32 lane-strided partial sums
+//                   folded pairwise, division (Kernels.Softmax)
+//   k_attn_pv       ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
+// One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
+// the G query heads sharing that KV head, so each key and value row is read
+// once per CTA for all of them. Scores live in a scratch buffer laid out per
+// request as [head][position][key] (S x S per head).
+
 __global__ void __launch_bounds__(att::THREADS, 2)
-k_attn_scores(const float *__restrict__ q, const float *__restrict__ k, float *__restrict__ scores,
+k_attn_scores(const float *__restrict__ q, const float *__restrict__ kc, float *__restrict__ scores,
               const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
               const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads, float scale) {
     using namespace att;
     extern __shared__ float sm[];
-    float *Qs = sm;            // R x LD, chain-major dims
-    float *Ks = sm + R * LD;   // KT x LD
+    float *Qs = sm;  // R x LD, chain-major dims; then two KT x LD key tiles
     const int G = n_heads / n_kv_heads, QT = R / G;
     const int2 wk = work[blockIdx.x];
     const int h = blockIdx.y, r = wk.x, q0 = wk.y;
@@ -91,20 +101,32 @@ k_attn_scores(const float *__restrict__ q, const float *__restrict__ k, float *_
     const int64_t start = req_start[r], base = req_base[r];
     const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
     const int tid = threadIdx.x;
+    const int qend = min(q0 + QT, S);
+    const uint32_t kbase = (uint32_t)__cvta_generic_to_shared(sm + R * LD);
+    // keys arrive already in chain-major order, 16 bytes at a time
+    auto load = [&](int st, int kt0) {
+#pragma unroll
+        for (int it = 0; it < KT * (HD / 4) / THREADS; it++) {
+            const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
+            const bool ok = p < qend;
+            cp_async16(kbase + (uint32_t)(st * KT * LD + kk * LD + c4 * 4) * 4,
+                       ok ? kc + (start + p) * kvdim + (int64_t)h * HD + c4 * 4 : kc, ok);
+        }
+    };
+    load(0, 0);
+    cp_async_commit();
     for (int idx = tid; idx < R * HD; idx += THREADS) {
         int row = idx / HD, d = idx % HD, i = row / G, g = row % G, tok = q0 + i;
         Qs[row * LD + chain_pos(d)] = tok < S ? q[(start + tok) * qdim + (int64_t)(h * G + g) * HD + d] : 0.0f;
     }
     const int warp = tid >> 5, lane = tid & 31;
     const int rl = lane >> 3, kl = lane & 7;  // rows warp*16 + rl + 4a, keys kl + 8b
-    const int qend = min(q0 + QT, S);
-    for (int kt0 = 0; kt0 < qend; kt0 += KT) {
+    for (int kt0 = 0, st = 0; kt0 < qend; kt0 += KT, st ^= 1) {
+        if (kt0 + KT < qend) load(st ^ 1, kt0 + KT);
+        cp_async_commit();
+        cp_async_wait1();
         __syncthreads();
-        for (int idx = tid; idx < KT * HD; idx += THREADS) {
-            int kk = idx / HD, d = idx % HD, p = kt0 + kk;
-            Ks[kk * LD + chain_pos(d)] = p < S ? k[(start + p) * kvdim + (int64_t)h * HD + d] : 0.0f;
-        }
-        __syncthreads();
+        const float *Ks = sm + R * LD + st * KT * LD;
         float e0[16], e4[16], T[16], U[16];
         auto chain = [&](int j, float (&c)[16]) {
 #pragma unroll
@@ -158,6 +180,7 @@ k_attn_scores(const float *__restrict__ q, const float *__restrict__ k, float *_
                 if (p <= pt) dst[p] = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), scale);
             }
         }
+        __syncthreads();
     }
 }
 
@@ -300,18 +323,18 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
     }
 }
 
-cudaError_t launch_attention(const float *q, const float *k, const float *v, float *ctx, float *scores,
+cudaError_t launch_attention(const float *q, const float *kc, const float *v, float *ctx, float *scores,
                              const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
                              const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s) {
     using namespace att;
     if (n_work == 0) return cudaSuccess;
     if (head_dim != HD || n_heads % n_kv_heads || R % (n_heads / n_kv_heads)) return cudaErrorInvalidValue;
-    const size_t smem_s = (size_t)(R + KT) * LD * 4, smem_pv = (size_t)2 * (PKT * LD + R * LDP) * 4;
+    const size_t smem_s = (size_t)(R + 2 * KT) * LD * 4, smem_pv = (size_t)2 * (PKT * LD + R * LDP) * 4;
     cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)n_work, (unsigned)n_kv_heads);
-    k_attn_scores<<<grid, THREADS, smem_s, s>>>(q, k, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
+    k_attn_scores<<<grid, THREADS, smem_s, s>>>(q, kc, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
                                                  scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_attn_softmax<<<grid, THREADS, 0, s>>>(scores, work, req_len, req_base, n_heads, n_kv_heads);
