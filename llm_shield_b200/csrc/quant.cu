@@ -27,39 +27,11 @@ __global__ void k_quantize(const float *__restrict__ x, int64_t M, int64_t K, in
     }
 }
 
-// One thread per 32-block, the block's 32 values in registers: the same
-// operations as k_quantize (max |x|, d = max/127, inv = 1/d or 0,
-// q = rne(x*inv), sum q) without shuffles, the integers stored 16 bytes at a
-// time. With u, the values are first SwiGLU(g = x, u) exactly as k_swiglu
-// computes them (Kernels.cs:83-90), so the f32 product never reaches memory.
-__global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ x, const float *__restrict__ u,
-                                                       int64_t M, int64_t K, int64_t ldx, QAct q) {
+// IntegerGemm.Quantize (IntegerGemm.cs:97-138) of block b of row t, the 32
+// values in registers: scale, int8 and f16 integers (16-byte stores), d·Σq, Σq.
+__device__ __forceinline__ void store_quantized_block(const float (&v)[32], int64_t t, int64_t b, int64_t K,
+                                                      const QAct &q) {
     const int64_t nb = K / 32;
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= M * nb) return;
-    const int64_t t = idx / nb, b = idx % nb;
-    float v[32];
-    const float4 *src = reinterpret_cast<const float4 *>(x + t * ldx + b * 32);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float4 f = __ldg(src + i);
-        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
-    }
-    if (u) {
-        const float4 *us = reinterpret_cast<const float4 *>(u + t * ldx + b * 32);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float4 f = __ldg(us + i);
-            const float uu[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float gv = v[4 * i + e];
-                const float uv = __fmul_rn(gv, uu[e]);
-                const float sg = __frcp_rn(__fadd_rn(1.0f, shield_expf(-gv)));  // == 1/(1+e), correctly rounded
-                v[4 * i + e] = __fmul_rn(sg, uv);
-            }
-        }
-    }
     float m = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; i++) m = fmaxf(m, fabsf(v[i]));
@@ -97,6 +69,43 @@ __global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__
     q.da[so] = d;
     if (q.ds) q.ds[so] = __fmul_rn(d, (float)sum);
     if (q.sums) q.sums[so] = sum;
+}
+
+// One thread per 32-block, the block's 32 values in registers: the same
+// operations as k_quantize (max |x|, d = max/127, inv = 1/d or 0,
+// q = rne(x*inv), sum q) without shuffles, the integers stored 16 bytes at a
+// time. With u, the values are first SwiGLU(g = x, u) as Kernels.SwiGlu
+// (Kernels.cs:83-90) computes it: u = g*u, then sigmoid(g)*u with
+// sigmoid = 1/(1 + exp(-g)); the f32 product never reaches memory.
+__global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ x, const float *__restrict__ u,
+                                                       int64_t M, int64_t K, int64_t ldx, QAct q) {
+    const int64_t nb = K / 32;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * nb) return;
+    const int64_t t = idx / nb, b = idx % nb;
+    float v[32];
+    const float4 *src = reinterpret_cast<const float4 *>(x + t * ldx + b * 32);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float4 f = __ldg(src + i);
+        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+    }
+    if (u) {
+        const float4 *us = reinterpret_cast<const float4 *>(u + t * ldx + b * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 f = __ldg(us + i);
+            const float uu[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float gv = v[4 * i + e];
+                const float uv = __fmul_rn(gv, uu[e]);
+                const float sg = __frcp_rn(__fadd_rn(1.0f, shield_expf(-gv)));  // == 1/(1+e), correctly rounded
+                v[4 * i + e] = __fmul_rn(sg, uv);
+            }
+        }
+    }
+    store_quantized_block(v, t, b, K, q);
 }
 
 static bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -174,10 +183,71 @@ __global__ void k_rmsnorm_quant(const float *__restrict__ x, const int32_t *__re
     }
 }
 
+// The same RMSNorm + quantization with two rows per warp: lanes 0-15 and
+// 16-31 each run one row's 16 partial chains (coalesced 64-byte reads), fold
+// them in Vector.Sum order with shuffles, then each lane normalizes and
+// quantizes whole 32-blocks (blocks lane%16, +16, ...) from registers.
+// Needs K % 32 == 0 and 16-byte aligned rows.
+__global__ void __launch_bounds__(256) k_rmsnorm_quant_rows(const float *__restrict__ x,
+                                                            const int32_t *__restrict__ row_idx, int64_t M, int K,
+                                                            const float *__restrict__ w, float eps,
+                                                            float *__restrict__ y, QAct q) {
+    const int lane = threadIdx.x & 31, c = lane & 15;
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;  // row of this half-warp
+    const bool live = t < M;
+    const int64_t src = live ? (row_idx ? row_idx[t] : t) : 0;
+    const float *xr = x + src * (int64_t)K;
+    const int vec_end = K >= 16 ? (K / 16) * 16 : 0;
+    float acc = 0.0f;
+    if (live)
+        for (int i = c; i < vec_end; i += 16) acc = __fadd_rn(acc, __fmul_rn(xr[i], xr[i]));
+    // Vector.Sum of partials 0-7 (in lane 0 of the half) and 8-15 (in lane 8):
+    // ((e0+e4)+(e1+e5)) + ((e2+e6)+(e3+e7))
+    float v = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
+    const float hi = __shfl_down_sync(0xffffffffu, v, 8);
+    float scale = 0.0f;
+    if (c == 0 && live) {
+        double sum = 0.0;
+        if (vec_end > 0) sum = __dadd_rn((double)v, (double)hi);
+        for (int i = vec_end; i < K; i++) sum = __dadd_rn(sum, __dmul_rn((double)xr[i], (double)xr[i]));
+        const float ms = __double2float_rn(__ddiv_rn(sum, (double)K));
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    }
+    scale = __shfl_sync(0xffffffffu, scale, lane & 16);
+    if (!live) return;
+    const int nb = K / 32;
+    for (int b = c; b < nb; b += 16) {
+        float vals[32];
+        const float4 *xs = reinterpret_cast<const float4 *>(xr + b * 32);
+        const float4 *ws = reinterpret_cast<const float4 *>(w + b * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 xv = __ldg(xs + i), wv = __ldg(ws + i);
+            vals[4 * i + 0] = __fmul_rn(__fmul_rn(xv.x, scale), wv.x);
+            vals[4 * i + 1] = __fmul_rn(__fmul_rn(xv.y, scale), wv.y);
+            vals[4 * i + 2] = __fmul_rn(__fmul_rn(xv.z, scale), wv.z);
+            vals[4 * i + 3] = __fmul_rn(__fmul_rn(xv.w, scale), wv.w);
+        }
+        if (y) {
+            float4 *ys = reinterpret_cast<float4 *>(y + t * (int64_t)K + b * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++) ys[i] = make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);
+        }
+        store_quantized_block(vals, t, b, K, q);
+    }
+}
+
 cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
                                  float eps, float *y, const QAct &q, cudaStream_t s) {
     if (M == 0) return cudaSuccess;
-    k_rmsnorm_quant<<<(unsigned)M, 128, 0, s>>>(x, row_idx, K, w, eps, y, q);
+    if (K % 32 == 0 && aligned16(x) && aligned16(w) && aligned16(y) && aligned16(q.a8) && aligned16(q.a16)) {
+        const int64_t threads = M * 16;
+        k_rmsnorm_quant_rows<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, row_idx, M, K, w, eps, y, q);
+    } else {
+        k_rmsnorm_quant<<<(unsigned)M, 128, 0, s>>>(x, row_idx, K, w, eps, y, q);
+    }
     return cudaGetLastError();
 }
 
