@@ -462,7 +462,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
         gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
         count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 d.temp, nullptr, s), "rope q");
+                                 d.temp, b.ctx, s), "rope q");
         count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
                                  nullptr, b.kc, s), "rope k");
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
@@ -470,7 +470,9 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());
         for (const AttGroup &ag : groups) {
             d.timing.launches += 3;
-            check_launch(launch_attention(b.q, b.kc, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
+            // the chain-major queries live in ctx: a group's PV writes only its
+            // own requests' rows, which no later group's scores read
+            check_launch(launch_attention(b.ctx, b.kc, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
                                           d_rbase, c.n_heads, c.n_kv_heads, c.head_dim, scale, s),
                          "attention");
         }

@@ -88,7 +88,7 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 // request as [head][position][key] (S x S per head).
 
 __global__ void __launch_bounds__(att::THREADS, 2)
-k_attn_scores(const float *__restrict__ q, const float *__restrict__ kc, float *__restrict__ scores,
+k_attn_scores(const float *__restrict__ qc, const float *__restrict__ kc, float *__restrict__ scores,
               const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
               const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads, float scale) {
     using namespace att;
@@ -113,12 +113,18 @@ k_attn_scores(const float *__restrict__ q, const float *__restrict__ kc, float *
                        ok ? kc + (start + p) * kvdim + (int64_t)h * HD + c4 * 4 : kc, ok);
         }
     };
+    // the CTA's query rows, also chain-major already, with the first key tile
+    const uint32_t qbase = (uint32_t)__cvta_generic_to_shared(Qs);
+#pragma unroll 4
+    for (int it = 0; it < R * (HD / 4) / THREADS; it++) {
+        const int idx = tid + it * THREADS, row = idx / (HD / 4), c4 = idx % (HD / 4);
+        const int i = row / G, g = row % G, tok = q0 + i;
+        const bool ok = tok < S;
+        cp_async16(qbase + (uint32_t)(row * LD + c4 * 4) * 4,
+                   ok ? qc + (start + tok) * qdim + (int64_t)(h * G + g) * HD + c4 * 4 : qc, ok);
+    }
     load(0, 0);
     cp_async_commit();
-    for (int idx = tid; idx < R * HD; idx += THREADS) {
-        int row = idx / HD, d = idx % HD, i = row / G, g = row % G, tok = q0 + i;
-        Qs[row * LD + chain_pos(d)] = tok < S ? q[(start + tok) * qdim + (int64_t)(h * G + g) * HD + d] : 0.0f;
-    }
     const int warp = tid >> 5, lane = tid & 31;
     const int rl = lane >> 3, kl = lane & 7;  // rows warp*16 + rl + 4a, keys kl + 8b
     for (int kt0 = 0, st = 0; kt0 < qend; kt0 += KT, st ^= 1) {
@@ -323,7 +329,7 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
     }
 }
 
-cudaError_t launch_attention(const float *q, const float *kc, const float *v, float *ctx, float *scores,
+cudaError_t launch_attention(const float *qc, const float *kc, const float *v, float *ctx, float *scores,
                              const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
                              const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s) {
@@ -334,7 +340,7 @@ cudaError_t launch_attention(const float *q, const float *kc, const float *v, fl
     cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)n_work, (unsigned)n_kv_heads);
-    k_attn_scores<<<grid, THREADS, smem_s, s>>>(q, kc, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
+    k_attn_scores<<<grid, THREADS, smem_s, s>>>(qc, kc, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
                                                  scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_attn_softmax<<<grid, THREADS, 0, s>>>(scores, work, req_len, req_base, n_heads, n_kv_heads);

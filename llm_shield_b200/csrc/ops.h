@@ -87,10 +87,11 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 // Causal GQA attention of a group of requests (three kernels, see forward_ops.cu).
 // work[i] = {request, first query token}; one CTA per (work item, KV head)
 // covers attention_rows_per_cta() query rows (tokens x the heads of a group).
-// kc: keys after RoPE in chain-major order (launch_rope's perm output).
+// qc, kc: queries and keys after RoPE in chain-major order (launch_rope's
+// perm output).
 // scores: scratch of n_heads * Σ len * score_row_stride(len) floats, request r
 // at req_base[r].
-cudaError_t launch_attention(const float *q, const float *kc, const float *v, float *ctx, float *scores,
+cudaError_t launch_attention(const float *qc, const float *kc, const float *v, float *ctx, float *scores,
                              const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
                              const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
                              cudaStream_t s);
