@@ -127,6 +127,32 @@ shield_status shield_score_batch(shield_ctx *ctx, const int32_t *ids, const int6
                                  float *score, float *logits, const volatile int32_t *cancel);
 
 /*
+ * The whole tied head at every request's last position: logits[r * vocab + v]
+ * for token v of request r (ShieldstralModerator.VerdictLogitsAsync /
+ * TopVerdictTokenAsync, ShieldstralModerator.cs:269-277,370-378).  Every
+ * entry is bit-identical to the same vocabulary row's logit from
+ * shield_score_batch (the row-subset head, MatMulTilingTests.cs:67-87).
+ * Requests, sharding and the cached prefix are handled as in
+ * shield_score_batch.
+ */
+shield_status shield_last_logits(shield_ctx *ctx, const int32_t *ids, const int64_t *offsets, int32_t n_req,
+                                 float *logits, const volatile int32_t *cancel);
+
+/*
+ * SystemPromptCache.CaptureAsync / Restore (SystemPromptCache.cs:51-75,
+ * KvCache.Snapshot/Restore, KvCache.cs:94-136) on the GPUs: forwards ids[0..n)
+ * once on every GPU of the context and keeps each layer's keys (after RoPE)
+ * and values there.  Afterwards, a request to shield_score_batch or
+ * shield_last_logits whose ids begin with these n ids and go beyond them
+ * forwards only the rest, attending to the cached prefix; its results are
+ * bit-identical to forwarding it whole (SystemPromptCacheTests.cs:41-74).
+ * Other requests are forwarded whole.  n = 0 drops the cache; so do
+ * shield_set_config and shield_upload_tensor (the weights changed).
+ * SHIELD_ERR_RANGE if n >= max_positions.
+ */
+shield_status shield_set_prefix(shield_ctx *ctx, const int32_t *ids, int32_t n);
+
+/*
  * QuantMatMul.ForwardAsync / ForwardRowsAsync (Numerics/QuantMatMul.cs:71-110)
  * on one GPU of the context, host buffers in and out:
  *   y[t, i] = dot(x[t, :], W[row(i), :]),  x: M x cols, y: M x n_out

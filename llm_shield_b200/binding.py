@@ -54,7 +54,7 @@ class ShieldTiming(C.Structure):
 
 EXPORTS = [
     "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
-    "shield_score_batch", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
+    "shield_score_batch", "shield_last_logits", "shield_set_prefix", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
     "shield_debug_block_dots",
     "shield_set_gemm_path", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
     "shield_device_stream", "shield_last_error",
@@ -79,6 +79,8 @@ def lib() -> C.CDLL:
         L.shield_set_config.argtypes = [P, C.POINTER(ShieldConfig)]
         L.shield_upload_tensor.argtypes = [P, C.c_char_p, C.c_uint32, C.c_int64, C.c_int64, P, C.c_size_t]
         L.shield_score_batch.argtypes = [P, P, P, C.c_int32, P, C.c_int32, C.c_int32, P, P, P, P, P]
+        L.shield_last_logits.argtypes = [P, P, P, C.c_int32, P, P]
+        L.shield_set_prefix.argtypes = [P, P, C.c_int32]
         L.shield_qmatmul.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, P, C.c_int32]
         L.shield_qmatmul_device.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
         L.shield_qmatmul_noalloc.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
@@ -169,13 +171,32 @@ class ShieldContext:
         for name, t in tensors.items():
             self.upload(name, t["type"], t["rows"], t["cols"], t["data"])
 
-    def score_batch(self, requests, verdict_ids, n_yes: int, cancel: np.ndarray | None = None):
-        """requests: list of int32 arrays. Returns (yes, no, score, logits)."""
+    @staticmethod
+    def _pack(requests):
         lens = np.array([len(r) for r in requests], np.int64)
         offsets = np.zeros(len(requests) + 1, np.int64)
         np.cumsum(lens, out=offsets[1:])
         ids = np.ascontiguousarray(np.concatenate(requests) if requests else np.zeros(0, np.int32), np.int32)
+        return ids, offsets
+
+    def score_batch(self, requests, verdict_ids, n_yes: int, cancel: np.ndarray | None = None):
+        """requests: list of int32 arrays. Returns (yes, no, score, logits)."""
+        ids, offsets = self._pack(requests)
         return self.score_packed(ids, offsets, verdict_ids, n_yes, cancel)
+
+    def last_logits(self, requests, cancel: np.ndarray | None = None) -> np.ndarray:
+        """The whole tied head at each request's last position: (n_req, vocab)."""
+        ids, offsets = self._pack(requests)
+        out = np.zeros((len(requests), self.spec.vocab), np.float32)
+        _check(lib().shield_last_logits(self._h, _p(ids), _p(offsets), len(requests), _p(out),
+                                        _p(cancel) if cancel is not None else None))
+        return out
+
+    def set_prefix(self, ids) -> None:
+        """Caches the keys and values of a shared prompt prefix on every GPU
+        (empty: drop the cache)."""
+        a = np.ascontiguousarray(ids, np.int32)
+        _check(lib().shield_set_prefix(self._h, _p(a) if a.size else None, a.size))
 
     def score_packed(self, ids: np.ndarray, offsets: np.ndarray, verdict_ids, n_yes: int, cancel=None):
         v = np.ascontiguousarray(verdict_ids, np.int32)

@@ -219,6 +219,10 @@ struct Device {
     float *cos_t = nullptr, *sin_t = nullptr, *temp = nullptr;
     Buffers buf;
     Scratch sx, sy, sa, sd;
+    Scratch sl;  // full-vocabulary logits of a chunk of last positions
+    // System-prompt prefix cache (SystemPromptCache.cs:51-75, KvCache.Snapshot):
+    // the prefix's keys after RoPE (chain-major) and values, [layer][pos][kv-dim].
+    float *pre_k = nullptr, *pre_v = nullptr;
     ~Device() {
         cudaSetDevice(ordinal);
         for (auto &kv : tensors) {
@@ -231,6 +235,8 @@ struct Device {
         dev_free(cos_t);
         dev_free(sin_t);
         dev_free(temp);
+        dev_free(pre_k);
+        dev_free(pre_v);
         buf.free_all();
         if (stream) cudaStreamDestroy(stream);
     }
@@ -246,7 +252,17 @@ struct Ctx {
     Config cfg;
     bool configured = false;
     int gemm_path = 0;
+    std::vector<int32_t> prefix;  // token ids whose KV every device holds (empty: none)
 };
+
+static void clear_prefix(Ctx &C) {
+    C.prefix.clear();
+    for (auto &d : C.devs) {
+        cudaSetDevice(d->ordinal);
+        dev_free(d->pre_k);
+        dev_free(d->pre_v);
+    }
+}
 
 // -------------------------------------------------------------- operations
 
@@ -352,15 +368,21 @@ static void check_device_error(Device &d) {
 struct Batch {  // one micro-batch of whole requests on one device
     std::vector<int32_t> req;     // indices into the caller's request list
     std::vector<int64_t> start;   // batch-local first token of each request
-    std::vector<int32_t> len;
+    std::vector<int32_t> len;     // tokens forwarded (after any cached prefix)
+    std::vector<int32_t> pre;     // cached prefix positions in front of them (0 or the prefix length)
     int64_t tokens = 0;
 };
 
 // MinistralModel.ForwardAsync (MinistralModel.cs:183-271) over a packed
-// micro-batch: every request starts at position 0 with an empty cache.
-// Leaves verdict logits (R x nv) in d.buf.h_logits after a stream sync.
+// micro-batch. A request with pre > 0 continues from the cached system-prompt
+// prefix (its tokens sit at positions pre, pre+1, ..); otherwise it starts at
+// position 0 with an empty cache. Leaves verdict logits (R x nv) in
+// d.buf.h_logits after a stream sync. full_logits (host, R x vocab): the whole
+// tied head at every last position instead. store_prefix: the batch is the
+// prefix alone; its per-layer keys and values are kept in d.pre_k / d.pre_v.
 static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batch &B, int nv,
-                          const volatile int32_t *cancel, int capture_layer, int capture_what, float *capture) {
+                          const volatile int32_t *cancel, int capture_layer, int capture_what, float *capture,
+                          float *full_logits = nullptr, bool store_prefix = false) {
     const Config &c = C.cfg;
     const int64_t M = B.tokens;
     const int R = (int)B.req.size();
@@ -368,15 +390,21 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     Buffers &b = d.buf;
     int32_t *hm = b.h_meta;
     int32_t *h_ids = hm, *h_pos = hm + M, *h_start = hm + 2 * M, *h_last = hm + 3 * M;
+    auto pre_of = [&](int r) { return B.pre.empty() ? 0 : B.pre[r]; };
+    bool any_pre = false;
     for (int r = 0; r < R; r++) {
         int64_t st = B.start[r];
+        const int32_t pre = pre_of(r);
+        any_pre |= pre > 0;
         for (int32_t p = 0; p < B.len[r]; p++) {
             h_ids[st + p] = ids_host[st + p];
-            h_pos[st + p] = p;
+            h_pos[st + p] = pre + p;
             h_start[st + p] = (int32_t)st;
         }
         h_last[r] = (int32_t)(st + B.len[r] - 1);
     }
+    const int64_t P = (int64_t)C.prefix.size();
+    if (any_pre && (!d.pre_k || !d.pre_v)) throw Error(SHIELD_ERR_STATE, "no prefix cached on this device");
     SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
     Timing &T = d.timing;
     cudaEvent_t f0 = nullptr, f1 = nullptr;
@@ -401,7 +429,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         int64_t used = 0;
         AttGroup cur{0, 0};
         for (int r = 0; r < R; r++) {
-            int64_t need = (int64_t)c.n_heads * B.len[r] * score_row_stride(B.len[r]);
+            int64_t need = (int64_t)c.n_heads * B.len[r] * score_row_stride(pre_of(r) + B.len[r]);
             if (used + need > b.scores_cap && cur.nw > 0) {
                 groups.push_back(cur);
                 cur = AttGroup{(int)(work.size() / 2), 0};
@@ -418,20 +446,21 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         if (cur.nw > 0) groups.push_back(cur);
     }
     const int n_work = (int)(work.size() / 2);
-    if (2 * n_work + 4 * R > 8 * b.cap) throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
+    if (2 * n_work + 5 * R + 1 > 8 * b.cap) throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
     int32_t *ha = b.h_att;
     memcpy(ha, work.data(), work.size() * 4);
-    int32_t *ha_start = ha + 2 * n_work, *ha_len = ha_start + R;
+    int32_t *ha_start = ha + 2 * n_work, *ha_len = ha_start + R, *ha_pre = ha_len + R;
     for (int r = 0; r < R; r++) {
         ha_start[r] = (int32_t)B.start[r];
         ha_len[r] = B.len[r];
+        ha_pre[r] = pre_of(r);
     }
-    int64_t base_off = (2 * n_work + 2 * R + 1) / 2 * 2;  // int64 array on an 8-byte boundary
+    int64_t base_off = (2 * n_work + 3 * R + 1) / 2 * 2;  // int64 array on an 8-byte boundary
     memcpy(ha + base_off, rbase.data(), (size_t)R * 8);
     size_t att_bytes = (size_t)(base_off + 2 * R) * 4;
     SHIELD_CUDA(cudaMemcpyAsync(b.att, ha, att_bytes, cudaMemcpyHostToDevice, s));
     const int2 *d_work = reinterpret_cast<const int2 *>(b.att);
-    const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R;
+    const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R, *d_rpre = d_rlen + R;
     const int64_t *d_rbase = reinterpret_cast<const int64_t *>(b.att + base_off);
 
     const Tensor &emb = d.get("token_embd.weight");
@@ -468,13 +497,32 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());
+        const int64_t layer_kv = (int64_t)l * P * c.kvdim();
+        if (store_prefix) {
+            SHIELD_CUDA(cudaMemcpyAsync(d.pre_k + layer_kv, b.kc, (size_t)(M * c.kvdim()) * 4, cudaMemcpyDeviceToDevice, s));
+            SHIELD_CUDA(cudaMemcpyAsync(d.pre_v + layer_kv, b.v, (size_t)(M * c.kvdim()) * 4, cudaMemcpyDeviceToDevice, s));
+        }
+        AttArgs A;
+        // the chain-major queries live in ctx: a group's PV writes only its
+        // own requests' rows, which no later group's scores read
+        A.qc = b.ctx;
+        A.kc = b.kc;
+        A.v = b.v;
+        A.ctx = b.ctx;
+        A.scores = b.scores;
+        A.req_start = d_rstart;
+        A.req_len = d_rlen;
+        A.req_pre = any_pre ? d_rpre : nullptr;
+        A.req_base = d_rbase;
+        A.pre_k = any_pre ? d.pre_k + layer_kv : nullptr;
+        A.pre_v = any_pre ? d.pre_v + layer_kv : nullptr;
+        A.n_heads = c.n_heads;
+        A.n_kv_heads = c.n_kv_heads;
+        A.scale = scale;
         for (const AttGroup &ag : groups) {
             d.timing.launches += 3;
-            // the chain-major queries live in ctx: a group's PV writes only its
-            // own requests' rows, which no later group's scores read
-            check_launch(launch_attention(b.ctx, b.kc, b.v, b.ctx, b.scores, d_work + ag.w0, ag.nw, d_rstart, d_rlen,
-                                          d_rbase, c.n_heads, c.n_kv_heads, c.head_dim, scale, s),
-                         "attention");
+            A.work = d_work + ag.w0;
+            check_launch(launch_attention(A, ag.nw, c.head_dim, s), "attention");
         }
         cap(l, SHIELD_ACT_ATTN_WEIGHTED, b.ctx, c.qdim());
         QAct qc = qact(b, M, c.qdim());
@@ -490,7 +538,29 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         gemm(C, d, wd, qf, b.h, c.hidden, EPI_ADD);
         cap(l, SHIELD_ACT_OUTPUT, b.h, c.hidden);
     }
-    if (nv > 0) {
+    if (full_logits) {
+        // last position of every request -> final norm -> the whole tied head
+        // (VerdictLogitsAsync, ShieldstralModerator.cs:269-277), in row chunks
+        const Tensor &on = d.get("output_norm.weight");
+        QAct qh = qact(b, R, c.hidden);
+        count_launch(d), check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
+        const int64_t V = c.vocab, nb = c.hidden / 32;
+        const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(R, ((int64_t)256 << 20) / (V * 4)));
+        float *dl = static_cast<float *>(d.sl.get((size_t)(chunk * V) * 4));
+        for (int64_t r0 = 0; r0 < R; r0 += chunk) {
+            QAct qc = qh;
+            qc.M = std::min<int64_t>(chunk, R - r0);
+            qc.a8 = qh.a8 + r0 * c.hidden;
+            qc.a16 = qh.a16 + r0 * c.hidden;
+            qc.da = qh.da + r0 * nb;
+            qc.ds = qh.ds + r0 * nb;
+            qc.sums = qh.sums + r0 * nb;
+            gemm(C, d, emb, qc, dl, V, EPI_STORE);
+            SHIELD_CUDA(cudaMemcpyAsync(full_logits + r0 * V, dl, (size_t)(qc.M * V) * 4, cudaMemcpyDeviceToHost, s));
+            if (T.level >= 1) T.d2h += qc.M * V * 4;
+        }
+        SHIELD_CUDA(cudaStreamSynchronize(s));
+    } else if (nv > 0) {
         // last position of every request -> final norm -> verdict rows of the tied head
         const Tensor &on = d.get("output_norm.weight");
         QAct qh = qact(b, R, c.hidden);
@@ -597,6 +667,7 @@ static void set_config(Ctx &C, const shield_config *in) {
     cfg.max_positions = c.max_positions > 0 ? c.max_positions : 8192;
     cfg.max_batch_tokens = c.max_batch_tokens > 0 ? c.max_batch_tokens : 16384;
     if (cfg.max_batch_tokens < cfg.max_positions) cfg.max_batch_tokens = cfg.max_positions;
+    clear_prefix(C);
     C.cfg = cfg;
     C.configured = true;
     for (auto &d : C.devs) {
@@ -610,6 +681,7 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
     if (!C.configured) throw Error(SHIELD_ERR_STATE, "shield_set_config must come before uploads");
     if (!name || !bytes) throw Error(SHIELD_ERR_ARG, "name and bytes must be non-null");
     if (rows <= 0 || cols <= 0) throw Error(SHIELD_ERR_ARG, "rows and cols must be positive");
+    clear_prefix(C);  // the cached prefix was computed with the old weights
     int64_t rb = row_bytes_of((int)type, cols);
     if (rb < 0) throw Error(SHIELD_ERR_UNSUPPORTED, std::string(name) + ": type " + std::to_string(type) +
                                                          " has no kernel, or cols is not a multiple of 32");
@@ -684,11 +756,12 @@ static void validate_ids(const Ctx &C, const int32_t *ids, int64_t n) {
 }
 
 // Packs a device's requests (in the given order) into micro-batches.
-static std::vector<Batch> make_batches(const Ctx &C, const std::vector<int32_t> &reqs, const int64_t *offsets) {
+static std::vector<Batch> make_batches(const Ctx &C, const std::vector<int32_t> &reqs, const int64_t *offsets,
+                                       const std::vector<int32_t> &pre) {
     std::vector<Batch> out;
     Batch cur;
     for (int32_t r : reqs) {
-        int32_t len = (int32_t)(offsets[r + 1] - offsets[r]);
+        int32_t len = (int32_t)(offsets[r + 1] - offsets[r]) - pre[r];
         if (cur.tokens + len > C.cfg.max_batch_tokens && !cur.req.empty()) {
             out.push_back(cur);
             cur = Batch();
@@ -696,27 +769,28 @@ static std::vector<Batch> make_batches(const Ctx &C, const std::vector<int32_t> 
         cur.req.push_back(r);
         cur.start.push_back(cur.tokens);
         cur.len.push_back(len);
+        cur.pre.push_back(pre[r]);
         cur.tokens += len;
     }
     if (!cur.req.empty()) out.push_back(cur);
     return out;
 }
 
-static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int32_t n_req, const int32_t *verdict,
-                        int32_t n_yes, int32_t n_no, float *yes, float *no, float *score, float *logits,
-                        const volatile int32_t *cancel) {
+// Requests sharded over the context's GPUs (longest-processing-time first),
+// micro-batched per GPU and forwarded; on_batch(device, batch) consumes each
+// micro-batch's results. A request whose ids start with the cached prefix and
+// go beyond it forwards only the rest (SystemPromptCache.cs:51-75); the
+// results are bit-identical either way.
+template <class OnBatch>
+static void forward_requests(Ctx &C, const int32_t *ids, const int64_t *offsets, int32_t n_req, int nv,
+                             const volatile int32_t *cancel, OnBatch on_batch, bool full_head) {
     if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
-    if (n_req < 0 || (n_req > 0 && (!ids || !offsets || !yes || !no || !score)))
-        throw Error(SHIELD_ERR_ARG, "null buffer");
-    if (n_yes <= 0 || n_no <= 0 || !verdict) throw Error(SHIELD_ERR_ARG, "need at least one yes and one no id");
-    int nv = n_yes + n_no;
-    if (nv > 64) throw Error(SHIELD_ERR_ARG, "at most 64 verdict ids");
-    for (int i = 0; i < nv; i++)
-        if (verdict[i] < 0 || verdict[i] >= C.cfg.vocab)
-            throw Error(SHIELD_ERR_RANGE, "verdict id " + std::to_string(verdict[i]) + " is outside the vocabulary");
+    if (n_req < 0 || (n_req > 0 && (!ids || !offsets))) throw Error(SHIELD_ERR_ARG, "null buffer");
     if (n_req == 0) return;
     if (offsets[0] != 0) throw Error(SHIELD_ERR_ARG, "offsets[0] must be 0");
+    const int32_t P = (int32_t)C.prefix.size();
     std::vector<std::pair<double, int32_t>> cost(n_req);
+    std::vector<int32_t> pre(n_req, 0);
     for (int32_t r = 0; r < n_req; r++) {
         int64_t len = offsets[r + 1] - offsets[r];
         if (len <= 0) throw Error(SHIELD_ERR_ARG, "request " + std::to_string(r) + " has no tokens");
@@ -724,7 +798,9 @@ static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int3
             throw Error(SHIELD_ERR_RANGE, "request " + std::to_string(r) + " has " + std::to_string(len) +
                                               " tokens, more than max_positions " +
                                               std::to_string(C.cfg.max_positions));
-        cost[r] = {(double)len * (1.0 + (double)len / 8192.0), r};
+        if (P > 0 && len > P && std::equal(C.prefix.begin(), C.prefix.end(), ids + offsets[r])) pre[r] = P;
+        const double own = (double)(len - pre[r]);
+        cost[r] = {own * (1.0 + (double)len / 8192.0), r};
     }
     validate_ids(C, ids, offsets[n_req]);
     // longest-processing-time-first assignment of requests to GPUs
@@ -751,19 +827,15 @@ static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int3
             Device &d = *C.devs[di];
             SHIELD_CUDA(cudaSetDevice(d.ordinal));
             ensure_buffers(C, d);
-            SHIELD_CUDA(cudaMemcpyAsync(d.buf.verdict, verdict, (size_t)nv * 4, cudaMemcpyHostToDevice, d.stream));
             std::vector<int32_t> packed;
-            for (const Batch &B : make_batches(C, assign[di], offsets)) {
+            std::vector<float> full;
+            for (const Batch &B : make_batches(C, assign[di], offsets, pre)) {
                 packed.resize(B.tokens);
                 for (size_t i = 0; i < B.req.size(); i++)
-                    memcpy(packed.data() + B.start[i], ids + offsets[B.req[i]], (size_t)B.len[i] * 4);
-                forward_batch(C, d, packed.data(), B, nv, cancel, -1, 0, nullptr);
-                for (size_t i = 0; i < B.req.size(); i++) {
-                    int32_t r = B.req[i];
-                    const float *v = d.buf.h_logits + i * nv;
-                    score_one(v, n_yes, n_no, score[r], yes[r], no[r]);
-                    if (logits) memcpy(logits + (int64_t)r * nv, v, (size_t)nv * 4);
-                }
+                    memcpy(packed.data() + B.start[i], ids + offsets[B.req[i]] + B.pre[i], (size_t)B.len[i] * 4);
+                if (full_head) full.resize(B.req.size() * (size_t)C.cfg.vocab);
+                forward_batch(C, d, packed.data(), B, nv, cancel, -1, 0, nullptr, full_head ? full.data() : nullptr);
+                on_batch(d, B, full_head ? full.data() : d.buf.h_logits);
             }
         } catch (const Error &e) {
             codes[di] = e.code;
@@ -782,6 +854,87 @@ static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int3
     }
     for (int di = 0; di < D; di++)
         if (codes[di] != SHIELD_OK) throw Error(codes[di], errors[di]);
+}
+
+static void score_batch(Ctx &C, const int32_t *ids, const int64_t *offsets, int32_t n_req, const int32_t *verdict,
+                        int32_t n_yes, int32_t n_no, float *yes, float *no, float *score, float *logits,
+                        const volatile int32_t *cancel) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (n_req < 0 || (n_req > 0 && (!ids || !offsets || !yes || !no || !score)))
+        throw Error(SHIELD_ERR_ARG, "null buffer");
+    if (n_yes <= 0 || n_no <= 0 || !verdict) throw Error(SHIELD_ERR_ARG, "need at least one yes and one no id");
+    int nv = n_yes + n_no;
+    if (nv > 64) throw Error(SHIELD_ERR_ARG, "at most 64 verdict ids");
+    for (int i = 0; i < nv; i++)
+        if (verdict[i] < 0 || verdict[i] >= C.cfg.vocab)
+            throw Error(SHIELD_ERR_RANGE, "verdict id " + std::to_string(verdict[i]) + " is outside the vocabulary");
+    if (n_req == 0) return;
+    for (auto &d : C.devs) {
+        SHIELD_CUDA(cudaSetDevice(d->ordinal));
+        ensure_buffers(C, *d);
+        SHIELD_CUDA(cudaMemcpyAsync(d->buf.verdict, verdict, (size_t)nv * 4, cudaMemcpyHostToDevice, d->stream));
+    }
+    forward_requests(
+        C, ids, offsets, n_req, nv, cancel,
+        [&](Device &, const Batch &B, const float *h_logits) {
+            for (size_t i = 0; i < B.req.size(); i++) {
+                int32_t r = B.req[i];
+                const float *v = h_logits + i * nv;
+                score_one(v, n_yes, n_no, score[r], yes[r], no[r]);
+                if (logits) memcpy(logits + (int64_t)r * nv, v, (size_t)nv * 4);
+            }
+        },
+        false);
+}
+
+// The whole tied head at every request's last position (VerdictLogitsAsync /
+// TopVerdictTokenAsync, ShieldstralModerator.cs:269-277,370-378).
+static void last_logits(Ctx &C, const int32_t *ids, const int64_t *offsets, int32_t n_req, float *logits,
+                        const volatile int32_t *cancel) {
+    if (n_req > 0 && !logits) throw Error(SHIELD_ERR_ARG, "null buffer");
+    const int64_t V = C.cfg.vocab;
+    forward_requests(
+        C, ids, offsets, n_req, 0, cancel,
+        [&](Device &, const Batch &B, const float *full) {
+            for (size_t i = 0; i < B.req.size(); i++)
+                memcpy(logits + (int64_t)B.req[i] * V, full + i * V, (size_t)V * 4);
+        },
+        true);
+}
+
+// SystemPromptCache.CaptureAsync (SystemPromptCache.cs:51-75): forwards the
+// prefix once per GPU and keeps every layer's keys and values; n = 0 drops it.
+static void set_prefix(Ctx &C, const int32_t *ids, int32_t n) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (n < 0 || (n > 0 && !ids)) throw Error(SHIELD_ERR_ARG, "bad prefix");
+    if (n >= C.cfg.max_positions)
+        throw Error(SHIELD_ERR_RANGE, "a prefix of " + std::to_string(n) + " tokens leaves no position below max_positions");
+    clear_prefix(C);
+    if (n == 0) return;
+    validate_ids(C, ids, n);
+    const Config &c = C.cfg;
+    for (auto &dp : C.devs) {
+        Device &d = *dp;
+        SHIELD_CUDA(cudaSetDevice(d.ordinal));
+        ensure_buffers(C, d);
+        const size_t floats = (size_t)c.n_layers * n * c.kvdim();
+        dev_alloc(d.pre_k, floats);
+        dev_alloc(d.pre_v, floats);
+        Batch B;
+        B.req = {0};
+        B.start = {0};
+        B.len = {n};
+        B.pre = {0};
+        B.tokens = n;
+        C.prefix.assign(ids, ids + n);  // forward_batch sizes the store from it
+        try {
+            forward_batch(C, d, ids, B, 0, nullptr, -1, 0, nullptr, nullptr, true);
+            SHIELD_CUDA(cudaStreamSynchronize(d.stream));
+        } catch (...) {
+            clear_prefix(C);
+            throw;
+        }
+    }
 }
 
 static Device &device_of(Ctx &C, int32_t device) {
@@ -914,6 +1067,21 @@ shield_status shield_score_batch(shield_ctx *ctx, const int32_t *ids, const int6
     });
 }
 
+shield_status shield_last_logits(shield_ctx *ctx, const int32_t *ids, const int64_t *offsets, int32_t n_req,
+                                 float *logits, const volatile int32_t *cancel) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        last_logits(ctx->c, ids, offsets, n_req, logits, cancel);
+    });
+}
+
+shield_status shield_set_prefix(shield_ctx *ctx, const int32_t *ids, int32_t n) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        set_prefix(ctx->c, ids, n);
+    });
+}
+
 shield_status shield_qmatmul(shield_ctx *ctx, int32_t device, const char *weight, const float *x, int64_t M,
                              float *y, const int32_t *row_ids, int32_t n_rows) {
     return guarded([&] {
@@ -1037,6 +1205,7 @@ shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int
         B.req = {0};
         B.start = {0};
         B.len = {n};
+        B.pre = {0};
         B.tokens = n;
         forward_batch(C, d, ids, B, 0, nullptr, layer, what, out);
     });

@@ -84,33 +84,58 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 //   k_attn_pv       ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
 // One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
 // the G query heads sharing that KV head, so each key and value row is read
-// once per CTA for all of them. Scores live in a scratch buffer laid out per
-// request as [head][position][key] (S x S per head).
+// once per CTA for all of them. A request's queries are its tokens in the
+// batch; its keys are the first pre positions of the cached prefix (pre_k,
+// pre_v: the system-prompt cache of SystemPromptCache.cs:51-75) followed by
+// its own tokens, so query token t sits at position pre + t. Scores live in a
+// scratch buffer laid out per request as [head][query][key], rows padded to
+// score_row_stride(pre + len) floats.
 
-__global__ void __launch_bounds__(att::THREADS, 2)
-k_attn_scores(const float *__restrict__ qc, const float *__restrict__ kc, float *__restrict__ scores,
-              const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
-              const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads, float scale) {
+// Per-request view shared by the three kernels.
+struct AttView {
+    int len, pre, q0, qend, kend;  // queries, prefix keys, this CTA's query range, keys it needs
+    int64_t start, base, ld;       // first batch row, scores offset, scores row stride
+};
+
+__device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
+    const int2 wk = A.work[blockIdx.x];
+    AttView w;
+    const int r = wk.x;
+    w.q0 = wk.y;
+    w.len = A.req_len[r];
+    w.pre = A.req_pre ? A.req_pre[r] : 0;
+    w.start = A.req_start[r];
+    w.base = A.req_base[r];
+    w.ld = score_ld(w.pre + w.len);
+    w.qend = min(w.q0 + QT, w.len);
+    w.kend = w.pre + w.qend;
+    return w;
+}
+
+// Row p of a request's keys or values: prefix row p, or its own token p - pre.
+__device__ __forceinline__ const float *kv_row(const float *own, const float *prefix, const AttView &w, int p,
+                                               int64_t kvdim) {
+    return p < w.pre ? prefix + (int64_t)p * kvdim : own + (w.start + p - w.pre) * kvdim;
+}
+
+__global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A) {
     using namespace att;
     extern __shared__ float sm[];
     float *Qs = sm;  // R x LD, chain-major dims; then two KT x LD key tiles
-    const int G = n_heads / n_kv_heads, QT = R / G;
-    const int2 wk = work[blockIdx.x];
-    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
-    const int S = req_len[r];
-    const int64_t start = req_start[r], base = req_base[r];
-    const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
+    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
+    const AttView w = att_view(A, QT);
+    const int h = blockIdx.y;
+    const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
     const int tid = threadIdx.x;
-    const int qend = min(q0 + QT, S);
     const uint32_t kbase = (uint32_t)__cvta_generic_to_shared(sm + R * LD);
     // keys arrive already in chain-major order, 16 bytes at a time
     auto load = [&](int st, int kt0) {
 #pragma unroll
         for (int it = 0; it < KT * (HD / 4) / THREADS; it++) {
             const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
-            const bool ok = p < qend;
+            const bool ok = p < w.kend;
             cp_async16(kbase + (uint32_t)(st * KT * LD + kk * LD + c4 * 4) * 4,
-                       ok ? kc + (start + p) * kvdim + (int64_t)h * HD + c4 * 4 : kc, ok);
+                       ok ? kv_row(A.kc, A.pre_k, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.kc, ok);
         }
     };
     // the CTA's query rows, also chain-major already, with the first key tile
@@ -118,17 +143,17 @@ k_attn_scores(const float *__restrict__ qc, const float *__restrict__ kc, float 
 #pragma unroll 4
     for (int it = 0; it < R * (HD / 4) / THREADS; it++) {
         const int idx = tid + it * THREADS, row = idx / (HD / 4), c4 = idx % (HD / 4);
-        const int i = row / G, g = row % G, tok = q0 + i;
-        const bool ok = tok < S;
+        const int i = row / G, g = row % G, tok = w.q0 + i;
+        const bool ok = tok < w.len;
         cp_async16(qbase + (uint32_t)(row * LD + c4 * 4) * 4,
-                   ok ? qc + (start + tok) * qdim + (int64_t)(h * G + g) * HD + c4 * 4 : qc, ok);
+                   ok ? A.qc + (w.start + tok) * qdim + (int64_t)(h * G + g) * HD + c4 * 4 : A.qc, ok);
     }
     load(0, 0);
     cp_async_commit();
     const int warp = tid >> 5, lane = tid & 31;
     const int rl = lane >> 3, kl = lane & 7;  // rows warp*16 + rl + 4a, keys kl + 8b
-    for (int kt0 = 0, st = 0; kt0 < qend; kt0 += KT, st ^= 1) {
-        if (kt0 + KT < qend) load(st ^ 1, kt0 + KT);
+    for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += KT, st ^= 1) {
+        if (kt0 + KT < w.kend) load(st ^ 1, kt0 + KT);
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
@@ -177,13 +202,13 @@ k_attn_scores(const float *__restrict__ qc, const float *__restrict__ kc, float 
         for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(e0[o], e4[o]));
 #pragma unroll
         for (int a = 0; a < 4; a++) {
-            const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, pt = q0 + i;
-            if (pt >= S) continue;
-            float *dst = scores + base + ((int64_t)(h * G + g) * S + pt) * score_ld(S);
+            const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, tok = w.q0 + i;
+            if (tok >= w.len) continue;
+            float *dst = A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld;
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const int p = kt0 + kl + 8 * b;
-                if (p <= pt) dst[p] = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), scale);
+                if (p <= w.pre + tok) dst[p] = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), A.scale);
             }
         }
         __syncthreads();
@@ -191,22 +216,17 @@ k_attn_scores(const float *__restrict__ qc, const float *__restrict__ kc, float 
 }
 
 // One warp per row at a time: rows of the CTA's 128-row tile, in turn.
-__global__ void __launch_bounds__(att::THREADS)
-k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const int32_t *__restrict__ req_len,
-               const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads) {
+__global__ void __launch_bounds__(att::THREADS) k_attn_softmax(const AttArgs A) {
     using namespace att;
-    const int G = n_heads / n_kv_heads, QT = R / G;
-    const int2 wk = work[blockIdx.x];
-    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
-    const int S = req_len[r];
-    const int64_t base = req_base[r];
+    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
+    const AttView w = att_view(A, QT);
+    const int h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qend = min(q0 + QT, S);
     for (int row = warp; row < R; row += THREADS / 32) {
-        const int i = row / G, g = row % G, pt = q0 + i;
-        if (pt >= S) continue;
-        const int limit = pt + 1;
-        float *s = scores + base + ((int64_t)(h * G + g) * S + pt) * score_ld(S);
+        const int i = row / G, g = row % G, tok = w.q0 + i;
+        if (tok >= w.len) continue;
+        const int limit = w.pre + tok + 1;
+        float *s = A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld;
         float mx = -INFINITY;
         for (int p = lane; p < limit; p += 32) mx = fmaxf(mx, s[p]);
         mx = warp_max(mx);
@@ -220,7 +240,7 @@ k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const 
         for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
         __syncwarp();
         for (int p = lane; p < limit; p += 32) s[p] = __fdiv_rn(s[p], sum);
-        for (int p = limit + lane; p < qend; p += 32) s[p] = 0.0f;  // keys the PV tile walks past
+        for (int p = limit + lane; p < w.kend; p += 32) s[p] = 0.0f;  // keys the PV tile walks past
         __syncwarp();
     }
 }
@@ -229,21 +249,15 @@ k_attn_softmax(float *__restrict__ scores, const int2 *__restrict__ work, const 
 // (MinistralModel.cs:372-440). Key tiles of V and of the softmax weights are
 // double-buffered in shared memory by cp.async; thread (tr, td) owns rows
 // tr + 32a and dims td*4 + 32e (a, e < 4).
-__global__ void __launch_bounds__(att::THREADS, 2)
-k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *__restrict__ ctx,
-          const int2 *__restrict__ work, const int32_t *__restrict__ req_start, const int32_t *__restrict__ req_len,
-          const int64_t *__restrict__ req_base, int n_heads, int n_kv_heads) {
+__global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
     using namespace att;
     extern __shared__ float sm[];
     constexpr int V_FLOATS = PKT * LD, W_FLOATS = R * LDP;
-    const int G = n_heads / n_kv_heads, QT = R / G;
-    const int2 wk = work[blockIdx.x];
-    const int h = blockIdx.y, r = wk.x, q0 = wk.y;
-    const int S = req_len[r];
-    const int64_t start = req_start[r], base = req_base[r], ld = score_ld(S);
-    const int64_t qdim = (int64_t)n_heads * HD, kvdim = (int64_t)n_kv_heads * HD;
+    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
+    const AttView w = att_view(A, QT);
+    const int h = blockIdx.y;
+    const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
     const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;
-    const int qend = min(q0 + QT, S);
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
     auto Vs = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS); };
     auto Ws = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS) + V_FLOATS; };
@@ -252,16 +266,17 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
 #pragma unroll
         for (int it = 0; it < PKT * (HD / 4) / THREADS; it++) {
             const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
-            const bool ok = p < qend;
-            cp_async16(vb + (uint32_t)(kk * LD + c4 * 4) * 4, ok ? v + (start + p) * kvdim + (int64_t)h * HD + c4 * 4 : v, ok);
+            const bool ok = p < w.kend;
+            cp_async16(vb + (uint32_t)(kk * LD + c4 * 4) * 4,
+                       ok ? kv_row(A.v, A.pre_v, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.v, ok);
         }
 #pragma unroll
         for (int it = 0; it < R * (PKT / 4) / THREADS; it++) {
             const int idx = tid + it * THREADS, row = idx / (PKT / 4), c4 = idx % (PKT / 4);
-            const int i = row / G, g = row % G, pt = q0 + i, p = kt0 + c4 * 4;
-            const bool ok = pt < S && p < qend;
+            const int i = row / G, g = row % G, tok = w.q0 + i, p = kt0 + c4 * 4;
+            const bool ok = tok < w.len && p < w.kend;
             cp_async16(wb + (uint32_t)(row * LDP + c4 * 4) * 4,
-                       ok ? scores + base + ((int64_t)(h * G + g) * S + pt) * ld + p : scores, ok);
+                       ok ? A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld + p : A.scores, ok);
         }
     };
     float c[4][16];
@@ -271,18 +286,18 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
         for (int e = 0; e < 16; e++) c[a][e] = 0.0f;
     load(0, 0);
     cp_async_commit();
-    for (int kt0 = 0, st = 0; kt0 < qend; kt0 += PKT, st ^= 1) {
-        if (kt0 + PKT < qend) load(st ^ 1, kt0 + PKT);
+    for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += PKT, st ^= 1) {
+        if (kt0 + PKT < w.kend) load(st ^ 1, kt0 + PKT);
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
         const float *V = Vs(st), *W = Ws(st);
-        const int kn = min(PKT, qend - kt0);
+        const int kn = min(PKT, w.kend - kt0);
         int kk = 0;
         for (; kk + 4 <= kn; kk += 4) {
-            float4 w[4];
+            float4 wt[4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) w[a] = *reinterpret_cast<const float4 *>(&W[(tr + 32 * a) * LDP + kk]);
+            for (int a = 0; a < 4; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + 32 * a) * LDP + kk]);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
 #pragma unroll
@@ -290,7 +305,7 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
                     const float4 vv = *reinterpret_cast<const float4 *>(&V[(kk + j) * LD + td * 4 + 32 * e]);
 #pragma unroll
                     for (int a = 0; a < 4; a++) {
-                        const float wa = j == 0 ? w[a].x : j == 1 ? w[a].y : j == 2 ? w[a].z : w[a].w;
+                        const float wa = j == 0 ? wt[a].x : j == 1 ? wt[a].y : j == 2 ? wt[a].z : wt[a].w;
                         c[a][4 * e + 0] = __fmaf_rn(vv.x, wa, c[a][4 * e + 0]);
                         c[a][4 * e + 1] = __fmaf_rn(vv.y, wa, c[a][4 * e + 1]);
                         c[a][4 * e + 2] = __fmaf_rn(vv.z, wa, c[a][4 * e + 2]);
@@ -319,9 +334,9 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
     }
 #pragma unroll
     for (int a = 0; a < 4; a++) {
-        const int row = tr + 32 * a, i = row / G, g = row % G, pt = q0 + i;
-        if (pt >= S) continue;
-        float *dst = ctx + (start + pt) * qdim + (int64_t)(h * G + g) * HD;
+        const int row = tr + 32 * a, i = row / G, g = row % G, tok = w.q0 + i;
+        if (tok >= w.len) continue;
+        float *dst = A.ctx + (w.start + tok) * qdim + (int64_t)(h * G + g) * HD;
 #pragma unroll
         for (int e = 0; e < 4; e++)
             *reinterpret_cast<float4 *>(dst + td * 4 + 32 * e) =
@@ -329,26 +344,21 @@ k_attn_pv(const float *__restrict__ v, const float *__restrict__ scores, float *
     }
 }
 
-cudaError_t launch_attention(const float *qc, const float *kc, const float *v, float *ctx, float *scores,
-                             const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
-                             const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
-                             cudaStream_t s) {
+cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, cudaStream_t s) {
     using namespace att;
     if (n_work == 0) return cudaSuccess;
-    if (head_dim != HD || n_heads % n_kv_heads || R % (n_heads / n_kv_heads)) return cudaErrorInvalidValue;
+    if (head_dim != HD || A.n_heads % A.n_kv_heads || R % (A.n_heads / A.n_kv_heads)) return cudaErrorInvalidValue;
     const size_t smem_s = (size_t)(R + 2 * KT) * LD * 4, smem_pv = (size_t)2 * (PKT * LD + R * LDP) * 4;
     cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)n_work, (unsigned)n_kv_heads);
-    k_attn_scores<<<grid, THREADS, smem_s, s>>>(qc, kc, scores, work, req_start, req_len, req_base, n_heads, n_kv_heads,
-                                                 scale);
+    dim3 grid((unsigned)n_work, (unsigned)A.n_kv_heads);
+    k_attn_scores<<<grid, THREADS, smem_s, s>>>(A);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_attn_softmax<<<grid, THREADS, 0, s>>>(scores, work, req_len, req_base, n_heads, n_kv_heads);
+    k_attn_softmax<<<grid, THREADS, 0, s>>>(A);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pv);
     if (e != cudaSuccess) return e;
-    k_attn_pv<<<grid, THREADS, smem_pv, s>>>(v, scores, ctx, work, req_start, req_len, req_base, n_heads,
-                                             n_kv_heads);
+    k_attn_pv<<<grid, THREADS, smem_pv, s>>>(A);
     return cudaGetLastError();
 }
 

@@ -87,14 +87,21 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 // Causal GQA attention of a group of requests (three kernels, see forward_ops.cu).
 // work[i] = {request, first query token}; one CTA per (work item, KV head)
 // covers attention_rows_per_cta() query rows (tokens x the heads of a group).
-// qc, kc: queries and keys after RoPE in chain-major order (launch_rope's
-// perm output).
-// scores: scratch of n_heads * Σ len * score_row_stride(len) floats, request r
-// at req_base[r].
-cudaError_t launch_attention(const float *qc, const float *kc, const float *v, float *ctx, float *scores,
-                             const int2 *work, int n_work, const int32_t *req_start, const int32_t *req_len,
-                             const int64_t *req_base, int n_heads, int n_kv_heads, int head_dim, float scale,
-                             cudaStream_t s);
+struct AttArgs {
+    const float *qc = nullptr;      // queries after RoPE, chain-major (launch_rope's perm output)
+    const float *kc = nullptr;      // keys after RoPE, chain-major
+    const float *v = nullptr;
+    float *ctx = nullptr;
+    float *scores = nullptr;        // n_heads * Σ len * score_row_stride(pre + len) floats
+    const int2 *work = nullptr;
+    const int32_t *req_start = nullptr, *req_len = nullptr;
+    const int32_t *req_pre = nullptr;   // cached prefix positions per request (nullptr: none)
+    const int64_t *req_base = nullptr;  // scores offset per request
+    const float *pre_k = nullptr, *pre_v = nullptr;  // this layer's cached prefix keys (chain-major), values
+    int n_heads = 0, n_kv_heads = 0;
+    float scale = 0.0f;
+};
+cudaError_t launch_attention(const AttArgs &args, int n_work, int head_dim, cudaStream_t s);
 int attention_rows_per_cta();
 // Scores of one (head, query) row are stored with a row stride rounded up to
 // 4 floats, so that every row starts on a 16-byte boundary.
