@@ -231,7 +231,10 @@ def main():
 
     ctx = binding.ShieldContext(1 << local)
     ctx.set_config(spec, max_positions=4096, max_batch_tokens=args.max_batch_tokens)
+    t_up = time.perf_counter()
     ctx.upload_model(tensors)
+    upload_s = time.perf_counter() - t_up
+    upload_bytes = sum(int(t["data"].nbytes) for t in tensors.values())
     vid = np.asarray(spec.verdict_ids, np.int32)
     nyes = len(spec.yes_ids)
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -316,6 +319,8 @@ def main():
                      "gemm_launches_profiled": g["gemm_launches"],
                      "gemm_share_of_forward": g["gemm_ms"] / g["forward_ms"] if g["forward_ms"] else None},
     }
+    line["upload"] = {"seconds": upload_s, "bytes": upload_bytes, "gb_per_s": upload_bytes / upload_s / 1e9,
+                      "what": "every GGUF tensor host->GPU, plus the scale planes and f16 layer copies built there"}
     line["clocks"] = clocks.summary()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec, tensors, ids, offsets)

@@ -220,6 +220,11 @@ struct Device {
     Buffers buf;
     Scratch sx, sy, sa, sd;
     Scratch sl;  // full-vocabulary logits of a chunk of last positions
+    // Upload staging: two pinned halves, so the host copy of one chunk
+    // overlaps the DMA of the other (GgufFile mmap -> pinned -> HBM).
+    static constexpr size_t STAGE_BYTES = (size_t)32 << 20;
+    uint8_t *stage = nullptr;
+    cudaEvent_t stage_free[2] = {nullptr, nullptr};
     // System-prompt prefix cache (SystemPromptCache.cs:51-75, KvCache.Snapshot):
     // the prefix's keys after RoPE (chain-major) and values, [layer][pos][kv-dim].
     float *pre_k = nullptr, *pre_v = nullptr;
@@ -237,6 +242,9 @@ struct Device {
         dev_free(temp);
         dev_free(pre_k);
         dev_free(pre_v);
+        if (stage) cudaFreeHost(stage);
+        for (auto &e : stage_free)
+            if (e) cudaEventDestroy(e);
         buf.free_all();
         if (stream) cudaStreamDestroy(stream);
     }
@@ -676,6 +684,55 @@ static void set_config(Ctx &C, const shield_config *in) {
     }
 }
 
+// Host bytes (pageable, e.g. the GGUF mmap) to device memory in 32 MB chunks
+// through the device's two pinned staging halves: the memcpy into one half
+// runs while the DMA out of the other is in flight.
+static void stage_to_device(Device &d, void *dst, const void *src, size_t nbytes) {
+    if (!d.stage) {
+        SHIELD_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&d.stage), 2 * Device::STAGE_BYTES, cudaHostAllocDefault));
+        for (auto &e : d.stage_free) SHIELD_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const uint8_t *in = static_cast<const uint8_t *>(src);
+    uint8_t *out = static_cast<uint8_t *>(dst);
+    for (size_t off = 0, k = 0; off < nbytes; off += Device::STAGE_BYTES, k ^= 1) {
+        const size_t n = std::min(Device::STAGE_BYTES, nbytes - off);
+        uint8_t *half = d.stage + k * Device::STAGE_BYTES;
+        SHIELD_CUDA(cudaEventSynchronize(d.stage_free[k]));  // its previous DMA has finished
+        memcpy(half, in + off, n);
+        SHIELD_CUDA(cudaMemcpyAsync(out + off, half, n, cudaMemcpyHostToDevice, d.stream));
+        SHIELD_CUDA(cudaEventRecord(d.stage_free[k], d.stream));
+    }
+}
+
+// Runs fn(device) for every GPU of the context, in parallel host threads when
+// there are several; the first failure is rethrown.
+template <class Fn>
+static void for_each_device(Ctx &C, Fn fn) {
+    const int D = (int)C.devs.size();
+    if (D == 1) {
+        fn(*C.devs[0]);
+        return;
+    }
+    std::vector<std::string> errors(D);
+    std::vector<shield_status> codes(D, SHIELD_OK);
+    std::vector<std::thread> th;
+    for (int di = 0; di < D; di++)
+        th.emplace_back([&, di] {
+            try {
+                fn(*C.devs[di]);
+            } catch (const Error &e) {
+                codes[di] = e.code;
+                errors[di] = e.what();
+            } catch (const std::exception &e) {
+                codes[di] = SHIELD_ERR_CUDA;
+                errors[di] = e.what();
+            }
+        });
+    for (auto &t : th) t.join();
+    for (int di = 0; di < D; di++)
+        if (codes[di] != SHIELD_OK) throw Error(codes[di], errors[di]);
+}
+
 static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_t cols, const void *bytes,
                    size_t nbytes) {
     if (!C.configured) throw Error(SHIELD_ERR_STATE, "shield_set_config must come before uploads");
@@ -698,9 +755,11 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
     if (is_vector && rows * cols != c.hidden) throw Error(SHIELD_ERR_SHAPE, n + " must have hidden elements");
     if (!is_vector && (type == T_F32 || type == T_F16))
         throw Error(SHIELD_ERR_UNSUPPORTED, n + ": float matrices are outside the integer path");
-    for (auto &dp : C.devs) {
-        Device &d = *dp;
+    // every GPU in its own host thread; bytes go through that GPU's pinned
+    // staging, and the planes and the f16 copy are built on its stream
+    auto one = [&](Device &d) {
         SHIELD_CUDA(cudaSetDevice(d.ordinal));
+        SHIELD_CUDA(cudaStreamSynchronize(d.stream));
         auto old = d.tensors.find(n);
         if (old != d.tensors.end()) {
             if (old->second.raw) cudaFree(old->second.raw);
@@ -727,7 +786,7 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
             SHIELD_CUDA(cudaMemcpy(t.vec, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
         } else {
             SHIELD_CUDA(cudaMalloc(&t.raw, nbytes + 64));
-            SHIELD_CUDA(cudaMemcpy(t.raw, bytes, nbytes, cudaMemcpyHostToDevice));
+            stage_to_device(d, t.raw, bytes, nbytes);
             t.w.type = (int)type;
             t.w.rows = rows;
             t.w.cols = cols;
@@ -735,17 +794,18 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
             t.w.data = static_cast<const uint8_t *>(t.raw);
             dev_alloc(t.w.scale_plane, (size_t)(rows * (cols / 32)));
             if (type == T_Q4_1 || type == T_Q5_1) dev_alloc(t.w.offset_plane, (size_t)(rows * (cols / 32)));
-            check_launch(launch_build_planes(t.w, nullptr), "scale planes");
+            check_launch(launch_build_planes(t.w, d.stream), "scale planes");
             // layer matrices also get an f16 copy for long token batches (the tied
             // embedding/head is only ever read a few rows at a time)
             if (n.compare(0, 4, "blk.") == 0 && cols % 256 == 0 && rows % 16 == 0) {
                 dev_alloc(t.w.w16, (size_t)(rows * cols));
-                check_launch(launch_unpack_f16(t.w, nullptr), "f16 weight copy");
+                check_launch(launch_unpack_f16(t.w, d.stream), "f16 weight copy");
             }
-            SHIELD_CUDA(cudaDeviceSynchronize());
+            SHIELD_CUDA(cudaStreamSynchronize(d.stream));
         }
         d.tensors.emplace(n, t);
-    }
+    };
+    for_each_device(C, one);
 }
 
 static void validate_ids(const Ctx &C, const int32_t *ids, int64_t n) {
