@@ -81,6 +81,29 @@ __device__ __forceinline__ int warp_sum_i(int v) {
 
 // Vector<float>.Sum of 8 lanes in the order the oracle states:
 // ((e0+e4)+(e1+e5)) + ((e2+e6)+(e3+e7)).
+// Two independent IEEE f32 operations per instruction (sm_100 packed f32x2):
+// each lane rounds exactly as the scalar __fmul_rn / __fmaf_rn would.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ float lo_f(uint64_t p) { return __uint_as_float((uint32_t)p); }
+__device__ __forceinline__ float hi_f(uint64_t p) { return __uint_as_float((uint32_t)(p >> 32)); }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ float vsum8(const float e[8]) {
     float s0 = __fadd_rn(e[0], e[4]), s1 = __fadd_rn(e[1], e[5]);
     float s2 = __fadd_rn(e[2], e[6]), s3 = __fadd_rn(e[3], e[7]);

@@ -259,7 +259,6 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
     const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
     const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
-    auto Vs = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS); };
     auto Ws = [&](int st) { return sm + st * (V_FLOATS + W_FLOATS) + V_FLOATS; };
     auto load = [&](int st, int kt0) {
         const uint32_t vb = sbase + (uint32_t)(st * (V_FLOATS + W_FLOATS)) * 4, wb = vb + V_FLOATS * 4;
@@ -279,11 +278,28 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
                        ok ? A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld + p : A.scores, ok);
         }
     };
-    float c[4][16];
+    // c2[a][2e + h]: dims td*4 + 32e + 2h + {0, 1} of row tr + 32a, as f32 pairs;
+    // each lane of a packed fma is the scalar fma(v[d], w, c[d])
+    uint64_t c2[4][8];
 #pragma unroll
     for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int e = 0; e < 16; e++) c[a][e] = 0.0f;
+        for (int e = 0; e < 8; e++) c2[a][e] = 0;
+    auto key = [&](uint32_t vrow, const float (&wa)[4]) {
+        uint64_t wd[4];
+#pragma unroll
+        for (int a = 0; a < 4; a++) wd[a] = pack2u(__float_as_uint(wa[a]), __float_as_uint(wa[a]));
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            uint64_t v0, v1;
+            asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "r"(vrow + (td * 4 + 32 * e) * 4));
+#pragma unroll
+            for (int a = 0; a < 4; a++) {
+                c2[a][2 * e] = fma2(v0, wd[a], c2[a][2 * e]);
+                c2[a][2 * e + 1] = fma2(v1, wd[a], c2[a][2 * e + 1]);
+            }
+        }
+    };
     load(0, 0);
     cp_async_commit();
     for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += PKT, st ^= 1) {
@@ -291,44 +307,24 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
-        const float *V = Vs(st), *W = Ws(st);
+        const uint32_t vs = sbase + (uint32_t)(st * (V_FLOATS + W_FLOATS)) * 4;
+        const float *W = Ws(st);
         const int kn = min(PKT, w.kend - kt0);
         int kk = 0;
         for (; kk + 4 <= kn; kk += 4) {
             float4 wt[4];
 #pragma unroll
             for (int a = 0; a < 4; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + 32 * a) * LDP + kk]);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float4 vv = *reinterpret_cast<const float4 *>(&V[(kk + j) * LD + td * 4 + 32 * e]);
-#pragma unroll
-                    for (int a = 0; a < 4; a++) {
-                        const float wa = j == 0 ? wt[a].x : j == 1 ? wt[a].y : j == 2 ? wt[a].z : wt[a].w;
-                        c[a][4 * e + 0] = __fmaf_rn(vv.x, wa, c[a][4 * e + 0]);
-                        c[a][4 * e + 1] = __fmaf_rn(vv.y, wa, c[a][4 * e + 1]);
-                        c[a][4 * e + 2] = __fmaf_rn(vv.z, wa, c[a][4 * e + 2]);
-                        c[a][4 * e + 3] = __fmaf_rn(vv.w, wa, c[a][4 * e + 3]);
-                    }
-                }
-            }
+            key(vs + (uint32_t)((kk + 0) * LD) * 4, {wt[0].x, wt[1].x, wt[2].x, wt[3].x});
+            key(vs + (uint32_t)((kk + 1) * LD) * 4, {wt[0].y, wt[1].y, wt[2].y, wt[3].y});
+            key(vs + (uint32_t)((kk + 2) * LD) * 4, {wt[0].z, wt[1].z, wt[2].z, wt[3].z});
+            key(vs + (uint32_t)((kk + 3) * LD) * 4, {wt[0].w, wt[1].w, wt[2].w, wt[3].w});
         }
         for (; kk < kn; kk++) {
             float wa[4];
 #pragma unroll
             for (int a = 0; a < 4; a++) wa[a] = W[(tr + 32 * a) * LDP + kk];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float4 vv = *reinterpret_cast<const float4 *>(&V[kk * LD + td * 4 + 32 * e]);
-#pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    c[a][4 * e + 0] = __fmaf_rn(vv.x, wa[a], c[a][4 * e + 0]);
-                    c[a][4 * e + 1] = __fmaf_rn(vv.y, wa[a], c[a][4 * e + 1]);
-                    c[a][4 * e + 2] = __fmaf_rn(vv.z, wa[a], c[a][4 * e + 2]);
-                    c[a][4 * e + 3] = __fmaf_rn(vv.w, wa[a], c[a][4 * e + 3]);
-                }
-            }
+            key(vs + (uint32_t)(kk * LD) * 4, wa);
         }
         __syncthreads();
     }
@@ -340,7 +336,7 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
 #pragma unroll
         for (int e = 0; e < 4; e++)
             *reinterpret_cast<float4 *>(dst + td * 4 + 32 * e) =
-                make_float4(c[a][4 * e], c[a][4 * e + 1], c[a][4 * e + 2], c[a][4 * e + 3]);
+                make_float4(lo_f(c2[a][2 * e]), hi_f(c2[a][2 * e]), lo_f(c2[a][2 * e + 1]), hi_f(c2[a][2 * e + 1]));
     }
 }
 

@@ -177,28 +177,6 @@ __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16])
 // of the row is set), which spreads 8 consecutive tokens over all banks.
 __device__ __forceinline__ int da_word(int T, int j) { return T * CHUNK + (j ^ (((T >> 2) & 1) << 2)); }
 
-// Two independent IEEE f32 operations per instruction (sm_100 packed f32x2):
-// each lane rounds exactly as the scalar __fmul_rn / __fmaf_rn would.
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
-}
-__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi) {
-    uint64_t d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
-    return d;
-}
-__device__ __forceinline__ float lo_f(uint64_t p) { return __uint_as_float((uint32_t)p); }
-__device__ __forceinline__ float hi_f(uint64_t p) { return __uint_as_float((uint32_t)(p >> 32)); }
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
 
 // Shared-memory loads at 32-bit shared addresses (kept in order with the
 // barrier waits that publish the data).
