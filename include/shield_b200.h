@@ -153,6 +153,31 @@ shield_status shield_last_logits(shield_ctx *ctx, const int32_t *ids, const int6
 shield_status shield_set_prefix(shield_ctx *ctx, const int32_t *ids, int32_t n);
 
 /*
+ * Incremental forwards on a KV cache, as MinistralModel.ForwardAsync appends
+ * to its KvCache (MinistralModel.cs:179-271, KvCache.cs) — the prefill-then-
+ * decode loop of Benchmark.cs:399-410.  A sequence is an empty cache for up
+ * to `capacity` positions (<= max_positions) on one GPU of the context.
+ * shield_seq_forward appends ids[offsets[i] .. offsets[i+1]) to sequence
+ * seqs[i] for i < n, all sequences in one batched forward per GPU (a decode
+ * step is one token per sequence), and writes each sequence's whole tied head
+ * at its new last position to logits[i * vocab ..] when logits is non-null.
+ * Every logit is bit-identical to forwarding the sequence's whole history in
+ * one call (shield_last_logits).  A sequence may appear once per call;
+ * SHIELD_ERR_RANGE when a sequence would exceed its capacity (nothing is
+ * appended then).  shield_upload_tensor empties every sequence (its keys and
+ * values came from the old weights); shield_set_config frees them all.
+ */
+shield_status shield_seq_create(shield_ctx *ctx, int32_t device, int32_t capacity, int64_t *seq);
+shield_status shield_seq_forward(shield_ctx *ctx, const int64_t *seqs, const int32_t *ids, const int64_t *offsets,
+                                 int32_t n, float *logits, const volatile int32_t *cancel);
+/* Positions the sequence holds (MinistralModel.CachedTokenCount). */
+shield_status shield_seq_length(shield_ctx *ctx, int64_t seq, int32_t *length);
+/* Empties the cache, keeping its memory (MinistralModel.ResetKvCache). */
+shield_status shield_seq_reset(shield_ctx *ctx, int64_t seq);
+/* Frees the sequence's device memory. */
+shield_status shield_seq_release(shield_ctx *ctx, int64_t seq);
+
+/*
  * QuantMatMul.ForwardAsync / ForwardRowsAsync (Numerics/QuantMatMul.cs:71-110)
  * on one GPU of the context, host buffers in and out:
  *   y[t, i] = dot(x[t, :], W[row(i), :]),  x: M x cols, y: M x n_out

@@ -54,7 +54,8 @@ class ShieldTiming(C.Structure):
 
 EXPORTS = [
     "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
-    "shield_score_batch", "shield_last_logits", "shield_set_prefix", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
+    "shield_score_batch", "shield_last_logits", "shield_set_prefix", "shield_seq_create", "shield_seq_forward",
+    "shield_seq_length", "shield_seq_reset", "shield_seq_release", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
     "shield_debug_block_dots",
     "shield_set_gemm_path", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
     "shield_device_stream", "shield_last_error",
@@ -81,6 +82,11 @@ def lib() -> C.CDLL:
         L.shield_score_batch.argtypes = [P, P, P, C.c_int32, P, C.c_int32, C.c_int32, P, P, P, P, P]
         L.shield_last_logits.argtypes = [P, P, P, C.c_int32, P, P]
         L.shield_set_prefix.argtypes = [P, P, C.c_int32]
+        L.shield_seq_create.argtypes = [P, C.c_int32, C.c_int32, C.POINTER(C.c_int64)]
+        L.shield_seq_forward.argtypes = [P, P, P, P, C.c_int32, P, P]
+        L.shield_seq_length.argtypes = [P, C.c_int64, C.POINTER(C.c_int32)]
+        L.shield_seq_reset.argtypes = [P, C.c_int64]
+        L.shield_seq_release.argtypes = [P, C.c_int64]
         L.shield_qmatmul.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, P, C.c_int32]
         L.shield_qmatmul_device.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
         L.shield_qmatmul_noalloc.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P]
@@ -191,6 +197,34 @@ class ShieldContext:
         _check(lib().shield_last_logits(self._h, _p(ids), _p(offsets), len(requests), _p(out),
                                         _p(cancel) if cancel is not None else None))
         return out
+
+    def seq_create(self, capacity: int, device: int = 0) -> int:
+        """An empty KV cache for up to `capacity` positions on one GPU."""
+        out = C.c_int64()
+        _check(lib().shield_seq_create(self._h, device, capacity, C.byref(out)))
+        return out.value
+
+    def seq_forward(self, seqs, chunks, want_logits: bool = True, cancel: np.ndarray | None = None):
+        """Appends chunks[i] (int32 ids) to sequence seqs[i]; returns the
+        (n, vocab) logits at each sequence's new last position."""
+        s = np.ascontiguousarray(seqs, np.int64)
+        ids, offsets = self._pack(chunks)
+        out = np.zeros((len(chunks), self.spec.vocab), np.float32) if want_logits else None
+        _check(lib().shield_seq_forward(self._h, _p(s), _p(ids), _p(offsets), len(chunks),
+                                        _p(out) if out is not None else None,
+                                        _p(cancel) if cancel is not None else None))
+        return out
+
+    def seq_length(self, seq: int) -> int:
+        out = C.c_int32()
+        _check(lib().shield_seq_length(self._h, seq, C.byref(out)))
+        return out.value
+
+    def seq_reset(self, seq: int) -> None:
+        _check(lib().shield_seq_reset(self._h, seq))
+
+    def seq_release(self, seq: int) -> None:
+        _check(lib().shield_seq_release(self._h, seq))
 
     def set_prefix(self, ids) -> None:
         """Caches the keys and values of a shared prompt prefix on every GPU

@@ -126,6 +126,11 @@ static void dev_free(T *&p) {
     p = nullptr;
 }
 
+// int32 words of attention metadata per token of capacity: the work list
+// (<= 2 per token + 2 per request) and per request start, len, pre (3), scores
+// base (2), cache keys, values and stride (6) and the append flag (1)
+constexpr int64_t ATT_INTS_PER_TOKEN = 16;
+
 struct Buffers {
     int64_t cap = 0;  // tokens
     float *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ctx = nullptr, *g = nullptr, *u = nullptr;
@@ -137,7 +142,7 @@ struct Buffers {
     int32_t *meta = nullptr;   // ids | pos | tok_start | last  (4 * cap)
     float *scores = nullptr;   // attention scores of a request group
     int64_t scores_cap = 0;    // floats
-    int32_t *att = nullptr;    // attention work list | request start | len | base  (8 * cap int32)
+    int32_t *att = nullptr;    // attention work list | start | len | pre | base | caches (ATT_INTS_PER_TOKEN * cap)
     int32_t *h_att = nullptr;  // pinned
     float *logits = nullptr;
     int32_t *verdict = nullptr;
@@ -228,6 +233,13 @@ struct Device {
     // System-prompt prefix cache (SystemPromptCache.cs:51-75, KvCache.Snapshot):
     // the prefix's keys after RoPE (chain-major) and values, [layer][pos][kv-dim].
     float *pre_k = nullptr, *pre_v = nullptr;
+    // Sequences for incremental forwards (MinistralModel.KvCache): each keeps
+    // its keys (after RoPE, chain-major) and values, [layer][position][kv-dim].
+    struct Sequence {
+        float *k = nullptr, *v = nullptr;
+        int32_t cap = 0, len = 0;
+    };
+    std::unordered_map<int64_t, Sequence> seqs;
     ~Device() {
         cudaSetDevice(ordinal);
         for (auto &kv : tensors) {
@@ -242,6 +254,10 @@ struct Device {
         dev_free(temp);
         dev_free(pre_k);
         dev_free(pre_v);
+        for (auto &kv : seqs) {
+            dev_free(kv.second.k);
+            dev_free(kv.second.v);
+        }
         if (stage) cudaFreeHost(stage);
         for (auto &e : stage_free)
             if (e) cudaEventDestroy(e);
@@ -261,6 +277,7 @@ struct Ctx {
     bool configured = false;
     int gemm_path = 0;
     std::vector<int32_t> prefix;  // token ids whose KV every device holds (empty: none)
+    int64_t next_seq = 1;         // sequence ids: (device << 48) | serial
 };
 
 static void clear_prefix(Ctx &C) {
@@ -269,6 +286,22 @@ static void clear_prefix(Ctx &C) {
         cudaSetDevice(d->ordinal);
         dev_free(d->pre_k);
         dev_free(d->pre_v);
+    }
+}
+
+// Cached keys and values are stale once the weights or the shapes change:
+// sequences are emptied (new weights) or freed (new configuration).
+static void drop_sequences(Ctx &C, bool free_them) {
+    for (auto &d : C.devs) {
+        cudaSetDevice(d->ordinal);
+        for (auto &kv : d->seqs) {
+            kv.second.len = 0;
+            if (free_them) {
+                dev_free(kv.second.k);
+                dev_free(kv.second.v);
+            }
+        }
+        if (free_them) d->seqs.clear();
     }
 }
 
@@ -357,8 +390,8 @@ static void ensure_buffers(Ctx &C, Device &d) {
     int64_t all = std::min<int64_t>((int64_t)1 << 30, (int64_t)c.n_heads * T * c.max_positions);
     d.buf.scores_cap = std::max(one, all);
     dev_alloc(d.buf.scores, (size_t)d.buf.scores_cap);
-    dev_alloc(d.buf.att, (size_t)(8 * T));
-    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_att, (size_t)(8 * T) * 4));
+    dev_alloc(d.buf.att, (size_t)(ATT_INTS_PER_TOKEN * T));
+    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_att, (size_t)(ATT_INTS_PER_TOKEN * T) * 4));
     d.buf.cap = T;
 }
 
@@ -376,8 +409,14 @@ static void check_device_error(Device &d) {
 struct Batch {  // one micro-batch of whole requests on one device
     std::vector<int32_t> req;     // indices into the caller's request list
     std::vector<int64_t> start;   // batch-local first token of each request
-    std::vector<int32_t> len;     // tokens forwarded (after any cached prefix)
-    std::vector<int32_t> pre;     // cached prefix positions in front of them (0 or the prefix length)
+    std::vector<int32_t> len;     // tokens forwarded (after any cached positions)
+    std::vector<int32_t> pre;     // cached positions in front of them
+    // where those cached positions live when not the system-prompt prefix: a
+    // sequence's cache (keys, values, floats per layer), and whether the
+    // forwarded tokens are appended to it (empty vectors: the prefix)
+    std::vector<const float *> ck, cv;
+    std::vector<int64_t> cstride;
+    std::vector<uint8_t> append;
     int64_t tokens = 0;
 };
 
@@ -412,7 +451,25 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         h_last[r] = (int32_t)(st + B.len[r] - 1);
     }
     const int64_t P = (int64_t)C.prefix.size();
-    if (any_pre && (!d.pre_k || !d.pre_v)) throw Error(SHIELD_ERR_STATE, "no prefix cached on this device");
+    // each request's cache: its sequence's, else the system-prompt prefix
+    std::vector<const float *> ck(R, nullptr), cv(R, nullptr);
+    std::vector<int64_t> cstride(R, 0);
+    std::vector<uint8_t> append(R, 0);
+    bool any_append = false;
+    for (int r = 0; r < R; r++) {
+        if (!B.ck.empty() && B.ck[r]) {
+            ck[r] = B.ck[r];
+            cv[r] = B.cv[r];
+            cstride[r] = B.cstride[r];
+            append[r] = B.append[r];
+            any_append |= append[r] != 0;
+        } else if (pre_of(r) > 0) {
+            if (!d.pre_k || !d.pre_v) throw Error(SHIELD_ERR_STATE, "no prefix cached on this device");
+            ck[r] = d.pre_k;
+            cv[r] = d.pre_v;
+            cstride[r] = P * c.kvdim();
+        }
+    }
     SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
     Timing &T = d.timing;
     cudaEvent_t f0 = nullptr, f1 = nullptr;
@@ -454,7 +511,8 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         if (cur.nw > 0) groups.push_back(cur);
     }
     const int n_work = (int)(work.size() / 2);
-    if (2 * n_work + 5 * R + 1 > 8 * b.cap) throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
+    if (2 * n_work + 12 * R + 4 > ATT_INTS_PER_TOKEN * b.cap)
+        throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
     int32_t *ha = b.h_att;
     memcpy(ha, work.data(), work.size() * 4);
     int32_t *ha_start = ha + 2 * n_work, *ha_len = ha_start + R, *ha_pre = ha_len + R;
@@ -463,13 +521,22 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         ha_len[r] = B.len[r];
         ha_pre[r] = pre_of(r);
     }
-    int64_t base_off = (2 * n_work + 3 * R + 1) / 2 * 2;  // int64 array on an 8-byte boundary
+    int64_t base_off = (2 * n_work + 3 * R + 1) / 2 * 2;  // int64 arrays on an 8-byte boundary
     memcpy(ha + base_off, rbase.data(), (size_t)R * 8);
-    size_t att_bytes = (size_t)(base_off + 2 * R) * 4;
+    const int64_t ck_off = base_off + 2 * R, cv_off = ck_off + 2 * R, cs_off = cv_off + 2 * R, ap_off = cs_off + 2 * R;
+    memcpy(ha + ck_off, ck.data(), (size_t)R * 8);
+    memcpy(ha + cv_off, cv.data(), (size_t)R * 8);
+    memcpy(ha + cs_off, cstride.data(), (size_t)R * 8);
+    memcpy(ha + ap_off, append.data(), (size_t)R);
+    size_t att_bytes = (size_t)(ap_off * 4 + R);
     SHIELD_CUDA(cudaMemcpyAsync(b.att, ha, att_bytes, cudaMemcpyHostToDevice, s));
     const int2 *d_work = reinterpret_cast<const int2 *>(b.att);
     const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R, *d_rpre = d_rlen + R;
     const int64_t *d_rbase = reinterpret_cast<const int64_t *>(b.att + base_off);
+    const float *const *d_ck = reinterpret_cast<const float *const *>(b.att + ck_off);
+    const float *const *d_cv = reinterpret_cast<const float *const *>(b.att + cv_off);
+    const int64_t *d_cs = reinterpret_cast<const int64_t *>(b.att + cs_off);
+    const uint8_t *d_app = reinterpret_cast<const uint8_t *>(b.att + ap_off);
 
     const Tensor &emb = d.get("token_embd.weight");
     count_launch(d), check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
@@ -520,13 +587,17 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         A.scores = b.scores;
         A.req_start = d_rstart;
         A.req_len = d_rlen;
-        A.req_pre = any_pre ? d_rpre : nullptr;
+        A.req_pre = d_rpre;
         A.req_base = d_rbase;
-        A.pre_k = any_pre ? d.pre_k + layer_kv : nullptr;
-        A.pre_v = any_pre ? d.pre_v + layer_kv : nullptr;
+        A.cache_k = d_ck;
+        A.cache_v = d_cv;
+        A.cache_stride = d_cs;
+        A.layer = l;
         A.n_heads = c.n_heads;
         A.n_kv_heads = c.n_kv_heads;
         A.scale = scale;
+        if (any_append)
+            count_launch(d), check_launch(launch_append_kv(A, d_app, R, M, (int)c.kvdim(), s), "append to KV caches");
         for (const AttGroup &ag : groups) {
             d.timing.launches += 3;
             A.work = d_work + ag.w0;
@@ -676,6 +747,7 @@ static void set_config(Ctx &C, const shield_config *in) {
     cfg.max_batch_tokens = c.max_batch_tokens > 0 ? c.max_batch_tokens : 16384;
     if (cfg.max_batch_tokens < cfg.max_positions) cfg.max_batch_tokens = cfg.max_positions;
     clear_prefix(C);
+    drop_sequences(C, true);
     C.cfg = cfg;
     C.configured = true;
     for (auto &d : C.devs) {
@@ -738,7 +810,8 @@ static void upload(Ctx &C, const char *name, uint32_t type, int64_t rows, int64_
     if (!C.configured) throw Error(SHIELD_ERR_STATE, "shield_set_config must come before uploads");
     if (!name || !bytes) throw Error(SHIELD_ERR_ARG, "name and bytes must be non-null");
     if (rows <= 0 || cols <= 0) throw Error(SHIELD_ERR_ARG, "rows and cols must be positive");
-    clear_prefix(C);  // the cached prefix was computed with the old weights
+    clear_prefix(C);  // cached keys and values were computed with the old weights
+    drop_sequences(C, false);
     int64_t rb = row_bytes_of((int)type, cols);
     if (rb < 0) throw Error(SHIELD_ERR_UNSUPPORTED, std::string(name) + ": type " + std::to_string(type) +
                                                          " has no kernel, or cols is not a multiple of 32");
@@ -997,6 +1070,139 @@ static void set_prefix(Ctx &C, const int32_t *ids, int32_t n) {
     }
 }
 
+// ---------------------------------------------------------- sequences
+
+static Device &device_of(Ctx &C, int32_t device);
+
+static Device::Sequence &sequence_of(Ctx &C, int64_t id, Device **dev) {
+    const int64_t di = id >> 48;
+    if (id <= 0 || di >= (int64_t)C.devs.size()) throw Error(SHIELD_ERR_ARG, "unknown sequence " + std::to_string(id));
+    Device &d = *C.devs[di];
+    auto it = d.seqs.find(id);
+    if (it == d.seqs.end()) throw Error(SHIELD_ERR_ARG, "unknown sequence " + std::to_string(id));
+    if (dev) *dev = &d;
+    return it->second;
+}
+
+// A new, empty KV cache for up to capacity positions on one GPU of the context.
+static int64_t seq_create(Ctx &C, int32_t device, int32_t capacity) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (capacity <= 0 || capacity > C.cfg.max_positions)
+        throw Error(SHIELD_ERR_RANGE, "sequence capacity must be in 1.." + std::to_string(C.cfg.max_positions));
+    Device &d = device_of(C, device);
+    Device::Sequence sq;
+    sq.cap = capacity;
+    const size_t floats = (size_t)C.cfg.n_layers * capacity * C.cfg.kvdim();
+    dev_alloc(sq.k, floats);
+    dev_alloc(sq.v, floats);
+    const int64_t id = ((int64_t)device << 48) | C.next_seq++;
+    d.seqs.emplace(id, sq);
+    return id;
+}
+
+// MinistralModel.ForwardAsync (MinistralModel.cs:179-271) on n sequences at
+// once: sequence i appends ids[offsets[i] .. offsets[i+1]) to its cache, every
+// new token attending to the cached positions and to the new ones before it;
+// logits (optional) gets each sequence's whole tied head at its new last
+// position. The results are bit-identical to forwarding each sequence's full
+// history in one piece.
+static void seq_forward(Ctx &C, const int64_t *seq, const int32_t *ids, const int64_t *offsets, int32_t n,
+                        float *logits, const volatile int32_t *cancel) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (n < 0 || (n > 0 && (!seq || !ids || !offsets))) throw Error(SHIELD_ERR_ARG, "null buffer");
+    if (n == 0) return;
+    if (offsets[0] != 0) throw Error(SHIELD_ERR_ARG, "offsets[0] must be 0");
+    const int D = (int)C.devs.size();
+    std::vector<std::vector<int32_t>> per_dev(D);
+    std::unordered_map<int64_t, int32_t> seen;
+    for (int32_t i = 0; i < n; i++) {
+        Device *dp = nullptr;
+        Device::Sequence &sq = sequence_of(C, seq[i], &dp);
+        if (!seen.emplace(seq[i], i).second)
+            throw Error(SHIELD_ERR_ARG, "sequence " + std::to_string(seq[i]) + " appears twice in one call");
+        const int64_t len = offsets[i + 1] - offsets[i];
+        if (len <= 0) throw Error(SHIELD_ERR_ARG, "sequence entry " + std::to_string(i) + " has no tokens");
+        if (sq.len + len > sq.cap)
+            throw Error(SHIELD_ERR_RANGE, "sequence " + std::to_string(seq[i]) + " would hold " +
+                                              std::to_string(sq.len + len) + " positions, more than its capacity " +
+                                              std::to_string(sq.cap));
+        per_dev[seq[i] >> 48].push_back(i);
+    }
+    validate_ids(C, ids, offsets[n]);
+    const int64_t V = C.cfg.vocab, stride_per_pos = C.cfg.kvdim();
+    std::vector<std::string> errors(D);
+    std::vector<shield_status> codes(D, SHIELD_OK);
+    auto run = [&](int di) {
+        try {
+            Device &d = *C.devs[di];
+            SHIELD_CUDA(cudaSetDevice(d.ordinal));
+            ensure_buffers(C, d);
+            const std::vector<int32_t> &mine = per_dev[di];
+            size_t k = 0;
+            std::vector<int32_t> packed;
+            std::vector<float> full;
+            while (k < mine.size()) {
+                Batch B;
+                while (k < mine.size()) {
+                    const int32_t i = mine[k];
+                    const int32_t len = (int32_t)(offsets[i + 1] - offsets[i]);
+                    if (B.tokens + len > C.cfg.max_batch_tokens && !B.req.empty()) break;
+                    Device::Sequence &sq = d.seqs.at(seq[i]);
+                    B.req.push_back(i);
+                    B.start.push_back(B.tokens);
+                    B.len.push_back(len);
+                    B.pre.push_back(sq.len);
+                    B.ck.push_back(sq.k);
+                    B.cv.push_back(sq.v);
+                    B.cstride.push_back((int64_t)sq.cap * stride_per_pos);
+                    B.append.push_back(1);
+                    B.tokens += len;
+                    k++;
+                }
+                packed.resize(B.tokens);
+                for (size_t j = 0; j < B.req.size(); j++)
+                    memcpy(packed.data() + B.start[j], ids + offsets[B.req[j]], (size_t)B.len[j] * 4);
+                full.resize(B.req.size() * (size_t)V);
+                forward_batch(C, d, packed.data(), B, 0, cancel, -1, 0, nullptr, full.data());
+                for (size_t j = 0; j < B.req.size(); j++) {
+                    d.seqs.at(seq[B.req[j]]).len += B.len[j];
+                    if (logits) memcpy(logits + (int64_t)B.req[j] * V, full.data() + j * V, (size_t)V * 4);
+                }
+            }
+        } catch (const Error &e) {
+            codes[di] = e.code;
+            errors[di] = e.what();
+        } catch (const std::exception &e) {
+            codes[di] = SHIELD_ERR_CUDA;
+            errors[di] = e.what();
+        }
+    };
+    if (D == 1) {
+        run(0);
+    } else {
+        std::vector<std::thread> th;
+        for (int di = 0; di < D; di++)
+            if (!per_dev[di].empty()) th.emplace_back(run, di);
+        for (auto &t : th) t.join();
+    }
+    for (int di = 0; di < D; di++)
+        if (codes[di] != SHIELD_OK) throw Error(codes[di], errors[di]);
+}
+
+static void seq_reset(Ctx &C, int64_t id) { sequence_of(C, id, nullptr).len = 0; }
+
+static void seq_release(Ctx &C, int64_t id) {
+    Device *d = nullptr;
+    Device::Sequence &sq = sequence_of(C, id, &d);
+    SHIELD_CUDA(cudaSetDevice(d->ordinal));
+    SHIELD_CUDA(cudaStreamSynchronize(d->stream));
+    dev_free(sq.k);
+    dev_free(sq.v);
+    d->seqs.erase(id);
+}
+
+static int32_t seq_length(Ctx &C, int64_t id) { return sequence_of(C, id, nullptr).len; }
+
 static Device &device_of(Ctx &C, int32_t device) {
     if (device < 0 || device >= (int32_t)C.devs.size())
         throw Error(SHIELD_ERR_RANGE, "device index " + std::to_string(device) + " is outside the context");
@@ -1132,6 +1338,42 @@ shield_status shield_last_logits(shield_ctx *ctx, const int32_t *ids, const int6
     return guarded([&] {
         if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
         last_logits(ctx->c, ids, offsets, n_req, logits, cancel);
+    });
+}
+
+shield_status shield_seq_create(shield_ctx *ctx, int32_t device, int32_t capacity, int64_t *seq) {
+    return guarded([&] {
+        if (!ctx || !seq) throw Error(SHIELD_ERR_ARG, "null argument");
+        *seq = seq_create(ctx->c, device, capacity);
+    });
+}
+
+shield_status shield_seq_forward(shield_ctx *ctx, const int64_t *seqs, const int32_t *ids, const int64_t *offsets,
+                                 int32_t n, float *logits, const volatile int32_t *cancel) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        seq_forward(ctx->c, seqs, ids, offsets, n, logits, cancel);
+    });
+}
+
+shield_status shield_seq_length(shield_ctx *ctx, int64_t seq, int32_t *length) {
+    return guarded([&] {
+        if (!ctx || !length) throw Error(SHIELD_ERR_ARG, "null argument");
+        *length = seq_length(ctx->c, seq);
+    });
+}
+
+shield_status shield_seq_reset(shield_ctx *ctx, int64_t seq) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        seq_reset(ctx->c, seq);
+    });
+}
+
+shield_status shield_seq_release(shield_ctx *ctx, int64_t seq) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        seq_release(ctx->c, seq);
     });
 }
 

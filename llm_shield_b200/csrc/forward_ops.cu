@@ -85,16 +85,18 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 // One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
 // the G query heads sharing that KV head, so each key and value row is read
 // once per CTA for all of them. A request's queries are its tokens in the
-// batch; its keys are the first pre positions of the cached prefix (pre_k,
-// pre_v: the system-prompt cache of SystemPromptCache.cs:51-75) followed by
-// its own tokens, so query token t sits at position pre + t. Scores live in a
+// batch; its keys are the first pre positions of its cache (the system-prompt
+// cache of SystemPromptCache.cs:51-75, or the request's own sequence, as
+// MinistralModel.ForwardAsync attends to KvCache, MinistralModel.cs:183-271)
+// followed by its own tokens, so query token t sits at position pre + t. Scores live in a
 // scratch buffer laid out per request as [head][query][key], rows padded to
 // score_row_stride(pre + len) floats.
 
 // Per-request view shared by the three kernels.
 struct AttView {
-    int len, pre, q0, qend, kend;  // queries, prefix keys, this CTA's query range, keys it needs
+    int len, pre, q0, qend, kend;  // queries, cached keys, this CTA's query range, keys it needs
     int64_t start, base, ld;       // first batch row, scores offset, scores row stride
+    const float *ck, *cv;          // this layer's cached keys and values (pre > 0)
 };
 
 __device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
@@ -109,13 +111,19 @@ __device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
     w.ld = score_ld(w.pre + w.len);
     w.qend = min(w.q0 + QT, w.len);
     w.kend = w.pre + w.qend;
+    w.ck = w.cv = nullptr;
+    if (w.pre > 0) {
+        const int64_t off = (int64_t)A.layer * A.cache_stride[r];
+        w.ck = A.cache_k[r] + off;
+        w.cv = A.cache_v[r] + off;
+    }
     return w;
 }
 
-// Row p of a request's keys or values: prefix row p, or its own token p - pre.
-__device__ __forceinline__ const float *kv_row(const float *own, const float *prefix, const AttView &w, int p,
+// Row p of a request's keys or values: cached row p, or its own token p - pre.
+__device__ __forceinline__ const float *kv_row(const float *own, const float *cached, const AttView &w, int p,
                                                int64_t kvdim) {
-    return p < w.pre ? prefix + (int64_t)p * kvdim : own + (w.start + p - w.pre) * kvdim;
+    return p < w.pre ? cached + (int64_t)p * kvdim : own + (w.start + p - w.pre) * kvdim;
 }
 
 __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A) {
@@ -135,7 +143,7 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
             const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
             const bool ok = p < w.kend;
             cp_async16(kbase + (uint32_t)(st * KT * LD + kk * LD + c4 * 4) * 4,
-                       ok ? kv_row(A.kc, A.pre_k, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.kc, ok);
+                       ok ? kv_row(A.kc, w.ck, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.kc, ok);
         }
     };
     // the CTA's query rows, also chain-major already, with the first key tile
@@ -267,7 +275,7 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
             const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
             const bool ok = p < w.kend;
             cp_async16(vb + (uint32_t)(kk * LD + c4 * 4) * 4,
-                       ok ? kv_row(A.v, A.pre_v, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.v, ok);
+                       ok ? kv_row(A.v, w.cv, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.v, ok);
         }
 #pragma unroll
         for (int it = 0; it < R * (PKT / 4) / THREADS; it++) {
@@ -359,5 +367,37 @@ cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, cudaStr
 }
 
 int attention_rows_per_cta() { return att::R; }
+
+// One thread per 4 floats of a new key or value row; the row's request by
+// binary search over the requests' first rows.
+__global__ void k_append_kv(const AttArgs A, const uint8_t *__restrict__ append, int n_req, int64_t M, int kvdim) {
+    const int64_t per_row = kvdim / 4;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * per_row) return;
+    const int64_t t = idx / per_row;
+    const int c4 = (int)(idx % per_row);
+    int lo = 0, hi = n_req - 1;  // last request whose first row <= t
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (A.req_start[mid] <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    const int r = lo;
+    if (!append[r]) return;
+    const int64_t pos = A.req_pre[r] + (t - A.req_start[r]);
+    const int64_t off = (int64_t)A.layer * A.cache_stride[r] + pos * kvdim + c4 * 4;
+    const int64_t src = t * kvdim + c4 * 4;
+    *reinterpret_cast<float4 *>(const_cast<float *>(A.cache_k[r]) + off) = *reinterpret_cast<const float4 *>(A.kc + src);
+    *reinterpret_cast<float4 *>(const_cast<float *>(A.cache_v[r]) + off) = *reinterpret_cast<const float4 *>(A.v + src);
+}
+
+cudaError_t launch_append_kv(const AttArgs &A, const uint8_t *append, int n_req, int64_t M, int kvdim,
+                             cudaStream_t s) {
+    const int64_t n = M * (kvdim / 4);
+    if (n == 0 || n_req == 0) return cudaSuccess;
+    if (kvdim % 4) return cudaErrorInvalidValue;
+    k_append_kv<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(A, append, n_req, M, kvdim);
+    return cudaGetLastError();
+}
 
 }  // namespace shield

@@ -95,13 +95,23 @@ struct AttArgs {
     float *scores = nullptr;        // n_heads * Σ len * score_row_stride(pre + len) floats
     const int2 *work = nullptr;
     const int32_t *req_start = nullptr, *req_len = nullptr;
-    const int32_t *req_pre = nullptr;   // cached prefix positions per request (nullptr: none)
+    const int32_t *req_pre = nullptr;   // cached positions in front of each request (nullptr: none)
     const int64_t *req_base = nullptr;  // scores offset per request
-    const float *pre_k = nullptr, *pre_v = nullptr;  // this layer's cached prefix keys (chain-major), values
+    // per request with pre > 0: its cache (the system-prompt prefix or its own
+    // sequence), layer 0 row 0 of the keys (chain-major) and values, and the
+    // floats from one layer's rows to the next
+    const float *const *cache_k = nullptr, *const *cache_v = nullptr;
+    const int64_t *cache_stride = nullptr;
+    int layer = 0;
     int n_heads = 0, n_kv_heads = 0;
     float scale = 0.0f;
 };
 cudaError_t launch_attention(const AttArgs &args, int n_work, int head_dim, cudaStream_t s);
+// Appends the batch's new keys (chain-major) and values of one layer to the
+// caches of the requests with a non-null append[r]: rows req_start[r] + t go
+// to position req_pre[r] + t of that cache (KvCache.Append, KvCache.cs).
+cudaError_t launch_append_kv(const AttArgs &args, const uint8_t *append, int n_req, int64_t M, int kvdim,
+                             cudaStream_t s);
 int attention_rows_per_cta();
 // Scores of one (head, query) row are stored with a row stride rounded up to
 // 4 floats, so that every row starts on a 16-byte boundary.
