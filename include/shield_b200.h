@@ -226,13 +226,15 @@ shield_status shield_qmatmul_noalloc(shield_ctx *ctx, int32_t device, const char
 shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const char *weight, const float *x,
                                       int64_t M, int32_t *dots, int32_t path);
 
-/* Which GEMM kernel the context uses: 0 = automatic (tensor cores where the
- * shape allows; long token batches read a once-unpacked f16 copy of the
- * layer weights, short ones unpack the GGUF blocks on the fly), 1 = CUDA-core
- * kernel only, 2 = tensor cores unpacking GGUF blocks only, 3 = tensor cores
- * on the unpacked copy only. 2 and 3 fail with SHIELD_ERR_UNSUPPORTED on shapes
- * the tensor cores do not take; the raw/unpacked choice is process-wide.
- * For cross-checking the kernels against each other. */
+/* Which GEMM kernel the context uses: 0 = automatic (1..16 tokens: one warp
+ * per output row; otherwise tensor cores where the shape allows, long token
+ * batches reading a once-unpacked f16 copy of the layer weights, short ones
+ * unpacking the GGUF blocks on the fly), 1 = CUDA-core tiled kernel only,
+ * 2 = tensor cores unpacking GGUF blocks only, 3 = tensor cores on the
+ * unpacked copy only, 4 = the one-warp-per-row kernel only. 2, 3 and 4 fail
+ * with SHIELD_ERR_UNSUPPORTED on shapes their kernel does not take; the
+ * raw/unpacked choice is process-wide. For cross-checking the kernels against
+ * each other. */
 shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path);
 
 /* Intermediate tensors of one layer, named as MinistralModel's

@@ -323,7 +323,16 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
         if (e0) cudaEventRecord(e0, d.stream);
     }
     bool done = false;
-    if (C.gemm_path != 1 && gemm_tc_supports(W.w, q.M)) {
+    // 1..16 tokens: one warp per output row (decode steps, the last rows)
+    if ((C.gemm_path == 0 || C.gemm_path == 4) && gemv_small_supports(W.w, q.M)) {
+        cudaError_t e = launch_gemv_small(W.w, q, y, ldy, epi, d.stream);
+        if (e == cudaSuccess)
+            done = true;
+        else if (e != cudaErrorNotSupported)
+            check_launch(e, "few-token GEMM");
+    }
+    if (C.gemm_path == 4 && !done) throw Error(SHIELD_ERR_UNSUPPORTED, "the few-token GEMM does not take this shape");
+    if (!done && C.gemm_path != 1 && C.gemm_path != 4 && gemm_tc_supports(W.w, q.M)) {
         cudaError_t e = launch_gemm_tc(W.w, q, y, ldy, epi, d.buf.err ? d.buf.err : nullptr, d.stream);
         if (e == cudaSuccess)
             done = true;
@@ -1484,7 +1493,7 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
 shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path) {
     return guarded([&] {
         if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
-        if (path < 0 || path > 3) throw Error(SHIELD_ERR_ARG, "path must be 0, 1, 2 or 3");
+        if (path < 0 || path > 4) throw Error(SHIELD_ERR_ARG, "path must be 0, 1, 2, 3 or 4");
         ctx->c.gemm_path = path;
         gemm_tc_set_pre_min_tokens(path == 2 ? INT64_MAX : path == 3 ? 1 : -1);
     });

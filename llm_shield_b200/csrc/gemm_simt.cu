@@ -143,6 +143,134 @@ cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- few tokens
+//
+// A handful of tokens (decode steps, the last rows of a batch): one warp per
+// output row, so every weight byte is read once and the whole GPU works on one
+// launch. Lane l takes blocks l, l+32, .. of a 32-block chunk: it unpacks the
+// block to signed int8 weights, forms each token's exact dot with dp4a and the
+// scale product dw·da; the chunk's results go through shared memory so that
+// lane m then runs token m's chain over the chunk in block order,
+//   f = fma(float(i), dw·da, f)   (then f = fma(m_w, d_a·Σa, f) for Q4_1/Q5_1)
+// the same operations, in the same order, as every other GEMM here.
+constexpr int GEMV_WARPS = 4;
+constexpr int GEMV_MAX_TOKENS = 16;
+
+// bit i of the 4-bit x -> bit 4 of byte i (the Q5 fifth bits as 0x10 per byte)
+__device__ __forceinline__ uint32_t spread4_bits(uint32_t x) { return ((x * 0x00204081u) & 0x01010101u) << 4; }
+
+// One block to 8 words of 4 signed int8 weights w = u - z (element order),
+// read with 16-bit loads (blocks are 2-byte aligned).
+template <int TYPE>
+__device__ __forceinline__ void block_to_i8x4(const uint8_t *blk, int (&wq)[8]) {
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
+    if (TYPE == T_Q8_0) {
+#pragma unroll
+        for (int g = 0; g < 8; g++) wq[g] = (int)((uint32_t)h[1 + 2 * g] | ((uint32_t)h[2 + 2 * g] << 16));
+        return;
+    }
+    const uint16_t *qs = h + qs_offset(TYPE) / 2;
+    uint32_t qh = 0;
+    if (TYPE == T_Q5_0 || TYPE == T_Q5_1)
+        qh = (uint32_t)h[qh_offset(TYPE) / 2] | ((uint32_t)h[qh_offset(TYPE) / 2 + 1] << 16);
+    const uint32_t z = (uint32_t)zero_point(TYPE) * 0x01010101u;
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        const uint32_t q = (uint32_t)qs[2 * g] | ((uint32_t)qs[2 * g + 1] << 16);
+        uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;  // elements 4g.. and 16+4g..
+        if (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
+            lo |= spread4_bits((qh >> (4 * g)) & 0xFu);
+            hi |= spread4_bits((qh >> (16 + 4 * g)) & 0xFu);
+        }
+        wq[g] = (int)__vsub4(lo, z);
+        wq[4 + g] = (int)__vsub4(hi, z);
+    }
+}
+
+template <int TYPE, int EPI>
+__global__ void __launch_bounds__(GEMV_WARPS * 32)
+k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
+             const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds, int M,
+             float *__restrict__ y, int64_t ldy) {
+    constexpr bool OFF = has_offset(TYPE);
+    __shared__ int32_t s_dot[GEMV_WARPS][32][GEMV_MAX_TOKENS + 1];
+    __shared__ float s_p[GEMV_WARPS][32][GEMV_MAX_TOKENS + 1];
+    __shared__ float s_off[GEMV_WARPS][32];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)blockIdx.x * GEMV_WARPS + wid;
+    if (n >= rows) return;  // whole warp
+    const int64_t nb = K / 32;
+    const uint8_t *row = W + n * row_bytes;
+    float f = 0.0f;  // lane m < M: token m's output
+    for (int64_t c0 = 0; c0 < nb; c0 += 32) {
+        const int64_t b = c0 + lane;
+        if (b < nb) {
+            const uint8_t *blk = row + b * block_bytes(TYPE);
+            int wq[8];
+            block_to_i8x4<TYPE>(blk, wq);
+            const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
+            if (OFF) s_off[wid][lane] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+            for (int m = 0; m < M; m++) {
+                const int4 *a4 = reinterpret_cast<const int4 *>(A + (int64_t)m * K + b * 32);
+                const int4 x0 = a4[0], x1 = a4[1];
+                int acc = 0;
+                acc = __dp4a(wq[0], x0.x, acc);
+                acc = __dp4a(wq[1], x0.y, acc);
+                acc = __dp4a(wq[2], x0.z, acc);
+                acc = __dp4a(wq[3], x0.w, acc);
+                acc = __dp4a(wq[4], x1.x, acc);
+                acc = __dp4a(wq[5], x1.y, acc);
+                acc = __dp4a(wq[6], x1.z, acc);
+                acc = __dp4a(wq[7], x1.w, acc);
+                s_dot[wid][lane][m] = acc;
+                s_p[wid][lane][m] = __fmul_rn(dw, da[(int64_t)m * nb + b]);
+            }
+        }
+        __syncwarp();
+        if (lane < M) {
+            const int nblk = nb - c0 < 32 ? (int)(nb - c0) : 32;
+            for (int l = 0; l < nblk; l++) {
+                f = __fmaf_rn((float)s_dot[wid][l][lane], s_p[wid][l][lane], f);
+                if (OFF) f = __fmaf_rn(s_off[wid][l], ds[(int64_t)lane * nb + c0 + l], f);
+            }
+        }
+        __syncwarp();
+    }
+    if (lane < M) {
+        float *dst = y + (int64_t)lane * ldy + n;
+        *dst = EPI == EPI_ADD ? __fadd_rn(*dst, f) : f;
+    }
+}
+
+template <int TYPE>
+static void gemv_small_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s) {
+    const unsigned grid = (unsigned)((w.rows + GEMV_WARPS - 1) / GEMV_WARPS);
+    if (epi == EPI_ADD)
+        k_gemv_small<TYPE, EPI_ADD><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.da,
+                                                                     q.ds, (int)q.M, y, ldy);
+    else
+        k_gemv_small<TYPE, EPI_STORE><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8,
+                                                                       q.da, q.ds, (int)q.M, y, ldy);
+}
+
+bool gemv_small_supports(const DevWeight &w, int64_t M) {
+    return M >= 1 && M <= GEMV_MAX_TOKENS && w.cols % 32 == 0 && block_bytes(w.type) != 0;
+}
+
+cudaError_t launch_gemv_small(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s) {
+    if (!gemv_small_supports(w, q.M) || !q.a8 || reinterpret_cast<uintptr_t>(q.a8) % 16 || w.cols % 16)
+        return cudaErrorNotSupported;
+    switch (w.type) {
+    case T_Q4_0: gemv_small_t<T_Q4_0>(w, q, y, ldy, epi, s); break;
+    case T_Q4_1: gemv_small_t<T_Q4_1>(w, q, y, ldy, epi, s); break;
+    case T_Q5_0: gemv_small_t<T_Q5_0>(w, q, y, ldy, epi, s); break;
+    case T_Q5_1: gemv_small_t<T_Q5_1>(w, q, y, ldy, epi, s); break;
+    case T_Q8_0: gemv_small_t<T_Q8_0>(w, q, y, ldy, epi, s); break;
+    default: return cudaErrorNotSupported;
+    }
+    return cudaGetLastError();
+}
+
 // Raw per-block dots: one thread per (t, n, b).
 template <int TYPE>
 __global__ void k_block_dots(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,

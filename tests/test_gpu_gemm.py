@@ -68,6 +68,26 @@ def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
     np.testing.assert_array_equal(got, expect)
 
 
+@pytest.mark.parametrize("qtype", INT_TYPES)
+@pytest.mark.parametrize("rows,cols", [(100, 256), (256, 3072), (3072, 9216)])
+def test_few_token_kernel_bit_identical_to_oracle(ctx, qtype, rows, cols):
+    """Path 4, the one-warp-per-row kernel automatic below 17 tokens."""
+    w = random_weights(qtype, rows, cols, seed=3 * rows + qtype)
+    upload(ctx, "blk.0.attn_v.weight", qtype, rows, cols, w)
+    ctx.set_gemm_path(4)
+    try:
+        for tokens in (1, 2, 7, 16):
+            x = np.random.default_rng(tokens).uniform(-2, 2, (tokens, cols)).astype(np.float32)
+            got = ctx.qmatmul("blk.0.attn_v.weight", x, tokens, rows)
+            np.testing.assert_array_equal(got, oracle.qmatmul(qtype, w, rows, cols, x, tokens),
+                                          err_msg=f"{tokens} tokens")
+        with pytest.raises(binding.ShieldError) as e:
+            ctx.qmatmul("blk.0.attn_v.weight", np.zeros((17, cols), np.float32), 17, rows)
+        assert e.value.code == binding.ERR_UNSUPPORTED
+    finally:
+        ctx.set_gemm_path(0)
+
+
 @pytest.mark.parametrize("qtype", [synth.Q4_0, synth.Q5_0, synth.Q5_1, synth.Q8_0])
 @pytest.mark.parametrize("rows,cols", SWEEP_SHAPES)
 def test_sweep_shapes_match_oracle(ctx, qtype, rows, cols):
