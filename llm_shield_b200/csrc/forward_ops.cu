@@ -25,8 +25,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool v
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-// dim d of a head stored so that FMA chain j (dims j, j+8, ...) is contiguous
-__device__ __forceinline__ int chain_pos(int d) { return (d & 7) * (att::HD / 8) + (d >> 3); }
+// Where dim d of a head is stored for the attention ("chain-major"): the
+// score's 8 FMA chains (chain j: dims j, j+8, .., j+120) are taken in pairs
+// (j, j+4), j < 4, and pair j's 32 floats are its two chains interleaved step
+// by step: dims j, j+4, j+8, j+12, .., so one 64-bit load holds the operands of
+// both chains at one step, for one packed f32x2 FMA.
+__device__ __forceinline__ int chain_pos(int d) { return (d & 3) * 32 + (d >> 3) * 2 + ((d >> 2) & 1); }
 
 // Rope.Apply (Rope.cs:112-135) on adjacent pairs, with cos/sin taken from the
 // per-position table the host computed (cos(pos·freq)·mscale), and the
@@ -166,48 +170,45 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
         cp_async_wait1();
         __syncthreads();
         const float *Ks = sm + R * LD + st * KT * LD;
-        float e0[16], e4[16], T[16], U[16];
-        auto chain = [&](int j, float (&c)[16]) {
+        // chains j and j+4 of each of the 4 x 4 (row, key) scores as one f32
+        // pair: each lane of a packed fma is the scalar fma of its chain
+        float T[16], U[16];
+        auto chain_pair = [&](int j, uint64_t (&c)[16]) {
 #pragma unroll
-            for (int o = 0; o < 16; o++) c[o] = 0.0f;
+            for (int o = 0; o < 16; o++) c[o] = 0;
 #pragma unroll
-            for (int st = 0; st < HD / 8; st += 4) {
+            for (int st = 0; st < 32; st += 4) {  // two steps of the pair per 16 bytes
                 float4 qa[4], kb[4];
 #pragma unroll
                 for (int a = 0; a < 4; a++)
-                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * (HD / 8) + st]);
+                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * 32 + st]);
 #pragma unroll
                 for (int b = 0; b < 4; b++)
-                    kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * (HD / 8) + st]);
+                    kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * 32 + st]);
 #pragma unroll
                 for (int a = 0; a < 4; a++)
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
-                        float &acc = c[a * 4 + b];
-                        acc = __fmaf_rn(qa[a].x, kb[b].x, acc);
-                        acc = __fmaf_rn(qa[a].y, kb[b].y, acc);
-                        acc = __fmaf_rn(qa[a].z, kb[b].z, acc);
-                        acc = __fmaf_rn(qa[a].w, kb[b].w, acc);
+                        uint64_t &acc = c[a * 4 + b];
+                        acc = fma2(pack2(qa[a].x, qa[a].y), pack2(kb[b].x, kb[b].y), acc);
+                        acc = fma2(pack2(qa[a].z, qa[a].w), pack2(kb[b].z, kb[b].w), acc);
                     }
             }
         };
-        // Vector.Sum order: ((e0+e4)+(e1+e5)) + ((e2+e6)+(e3+e7))
-        chain(0, e0);
-        chain(4, e4);
+        // Vector.Sum order: ((e0+e4)+(e1+e5)) + ((e2+e6)+(e3+e7)); pair j holds (ej, ej+4)
+        uint64_t c2[16];
+        chain_pair(0, c2);
 #pragma unroll
-        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(e0[o], e4[o]);
-        chain(1, e0);
-        chain(5, e4);
+        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(lo_f(c2[o]), hi_f(c2[o]));
+        chain_pair(1, c2);
 #pragma unroll
-        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(T[o], __fadd_rn(e0[o], e4[o]));
-        chain(2, e0);
-        chain(6, e4);
+        for (int o = 0; o < 16; o++) T[o] = __fadd_rn(T[o], __fadd_rn(lo_f(c2[o]), hi_f(c2[o])));
+        chain_pair(2, c2);
 #pragma unroll
-        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(e0[o], e4[o]);
-        chain(3, e0);
-        chain(7, e4);
+        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(lo_f(c2[o]), hi_f(c2[o]));
+        chain_pair(3, c2);
 #pragma unroll
-        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(e0[o], e4[o]));
+        for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(lo_f(c2[o]), hi_f(c2[o])));
 #pragma unroll
         for (int a = 0; a < 4; a++) {
             const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, tok = w.q0 + i;
