@@ -77,6 +77,19 @@ def step_slice(step, rank, world, batch):
     return idx
 
 
+def combine_ranks(dist, fwd_ms, e2e_ms, tokens, reqs, launches, device):
+    """The whole job's numbers: the slowest rank's device times (max), the
+    ranks' tokens, requests and kernel launches summed. dist None: one rank."""
+    if dist is None:
+        return fwd_ms, e2e_ms, tokens, reqs, launches
+    import torch
+    t = torch.tensor([fwd_ms, e2e_ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    c = torch.tensor([tokens, reqs, launches], dtype=torch.float64, device=device)
+    dist.all_reduce(c, op=dist.ReduceOp.SUM)
+    return float(t[0]), float(t[1]), int(c[0]), int(c[1]), int(c[2])
+
+
 def pack(ids, offsets, idx):
     parts = [ids[offsets[i]:offsets[i + 1]] for i in idx]
     lens = np.array([p.size for p in parts], np.int64)
@@ -274,15 +287,8 @@ def main():
     g = ctx.read_timing(reset=True)
     ctx.set_timing(0)
 
-    if dist:
-        t = torch.tensor([fwd_ms, e2e_ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        fwd_ms, e2e_ms = float(t[0]), float(t[1])
-        c = torch.tensor([tokens, reqs, tm["kernel_launches"]], dtype=torch.float64, device="cuda")
-        dist.all_reduce(c, op=dist.ReduceOp.SUM)
-        tokens, reqs, launches = int(c[0]), int(c[1]), int(c[2])
-    else:
-        launches = tm["kernel_launches"]
+    fwd_ms, e2e_ms, tokens, reqs, launches = combine_ranks(dist, fwd_ms, e2e_ms, tokens, reqs,
+                                                           tm["kernel_launches"], "cuda")
 
     hbm, bf16, src = measured_peaks()
     achieved = g["gemm_ops"] / (g["gemm_ms"] * 1e-3) / 1e12 if g["gemm_ms"] > 0 else 0.0
