@@ -240,6 +240,21 @@ struct Device {
         int32_t cap = 0, len = 0;
     };
     std::unordered_map<int64_t, Sequence> seqs;
+    // Captured decode steps, by batch shape (see forward_batch).
+    struct GraphEntry {
+        cudaGraphExec_t exec = nullptr;
+        float *d_logits = nullptr, *h_logits = nullptr;
+    };
+    std::unordered_map<std::string, GraphEntry> graphs;
+    bool no_graphs = false;  // a capture failed on this device: plain launches only
+    void clear_graphs() {
+        for (auto &kv : graphs) {
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+            if (kv.second.d_logits) cudaFree(kv.second.d_logits);
+            if (kv.second.h_logits) cudaFreeHost(kv.second.h_logits);
+        }
+        graphs.clear();
+    }
     ~Device() {
         cudaSetDevice(ordinal);
         for (auto &kv : tensors) {
@@ -258,6 +273,7 @@ struct Device {
             dev_free(kv.second.k);
             dev_free(kv.second.v);
         }
+        clear_graphs();
         if (stage) cudaFreeHost(stage);
         for (auto &e : stage_free)
             if (e) cudaEventDestroy(e);
@@ -294,6 +310,7 @@ static void clear_prefix(Ctx &C) {
 static void drop_sequences(Ctx &C, bool free_them) {
     for (auto &d : C.devs) {
         cudaSetDevice(d->ordinal);
+        d->clear_graphs();  // they hold the buffers' and the weights' addresses
         for (auto &kv : d->seqs) {
             kv.second.len = 0;
             if (free_them) {
@@ -438,7 +455,7 @@ struct Batch {  // one micro-batch of whole requests on one device
 // prefix alone; its per-layer keys and values are kept in d.pre_k / d.pre_v.
 static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batch &B, int nv,
                           const volatile int32_t *cancel, int capture_layer, int capture_what, float *capture,
-                          float *full_logits = nullptr, bool store_prefix = false) {
+                          float *full_logits = nullptr, bool store_prefix = false, bool graph = false) {
     const Config &c = C.cfg;
     const int64_t M = B.tokens;
     const int R = (int)B.req.size();
@@ -478,17 +495,6 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             cv[r] = d.pre_v;
             cstride[r] = P * c.kvdim();
         }
-    }
-    SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
-    Timing &T = d.timing;
-    cudaEvent_t f0 = nullptr, f1 = nullptr;
-    if (T.level >= 1) {
-        T.h2d += (3 * M + R) * 4;
-        T.tokens += M;
-        T.requests += R;
-        f0 = T.event();
-        f1 = T.event();
-        if (f0) cudaEventRecord(f0, s);
     }
     const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_last = b.meta + 3 * M;
 
@@ -538,7 +544,6 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     memcpy(ha + cs_off, cstride.data(), (size_t)R * 8);
     memcpy(ha + ap_off, append.data(), (size_t)R);
     size_t att_bytes = (size_t)(ap_off * 4 + R);
-    SHIELD_CUDA(cudaMemcpyAsync(b.att, ha, att_bytes, cudaMemcpyHostToDevice, s));
     const int2 *d_work = reinterpret_cast<const int2 *>(b.att);
     const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R, *d_rpre = d_rlen + R;
     const int64_t *d_rbase = reinterpret_cast<const int64_t *>(b.att + base_off);
@@ -546,6 +551,71 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     const float *const *d_cv = reinterpret_cast<const float *const *>(b.att + cv_off);
     const int64_t *d_cs = reinterpret_cast<const int64_t *>(b.att + cs_off);
     const uint8_t *d_app = reinterpret_cast<const uint8_t *>(b.att + ap_off);
+
+    // Everything from here on is stream work. A decode-shaped batch (graph)
+    // replays a CUDA graph captured the first time its shape was seen: the
+    // host arrays above are re-read from pinned memory by its copy nodes.
+    Timing &T = d.timing;
+    Device::GraphEntry *ge = nullptr;
+    bool capturing = false;
+    std::string graph_key;
+    const int saved_level = T.level;
+    if (graph) {
+        std::string key = std::to_string(M) + "/" + std::to_string(R) + "/" + std::to_string(nv) + "/" +
+                          (full_logits ? "f" : "-") + (any_append ? "a" : "-");
+        for (const AttGroup &ag : groups) key += "/" + std::to_string(ag.w0) + ":" + std::to_string(ag.nw);
+        auto it = d.graphs.find(key);
+        if (it != d.graphs.end()) {
+            ge = &it->second;
+            SHIELD_CUDA(cudaGraphLaunch(ge->exec, s));
+            SHIELD_CUDA(cudaStreamSynchronize(s));
+            check_device_error(d);
+            if (full_logits) memcpy(full_logits, ge->h_logits, (size_t)R * c.vocab * 4);
+            else if (nv > 0) memcpy(b.h_logits, ge->h_logits, (size_t)R * nv * 4);
+            return;
+        }
+        Device::GraphEntry e;
+        const size_t out_floats = (size_t)R * (full_logits ? c.vocab : nv);
+        dev_alloc(e.d_logits, std::max<size_t>(out_floats, 1));
+        SHIELD_CUDA(cudaMallocHost(reinterpret_cast<void **>(&e.h_logits), std::max<size_t>(out_floats, 1) * 4));
+        ge = &d.graphs.emplace(key, e).first->second;
+        graph_key = key;
+        T.level = 0;
+        SHIELD_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        capturing = true;
+    }
+    // a failure while capturing ends the capture and drops the half-made entry
+    struct CaptureGuard {
+        Device &d;
+        Timing &T;
+        bool &active;
+        const std::string &key;
+        int level;
+        ~CaptureGuard() {
+            if (!active) return;
+            cudaGraph_t g = nullptr;
+            cudaStreamEndCapture(d.stream, &g);
+            if (g) cudaGraphDestroy(g);
+            T.level = level;
+            auto it = d.graphs.find(key);
+            if (it != d.graphs.end()) {
+                if (it->second.d_logits) cudaFree(it->second.d_logits);
+                if (it->second.h_logits) cudaFreeHost(it->second.h_logits);
+                d.graphs.erase(it);
+            }
+        }
+    } guard{d, T, capturing, graph_key, saved_level};
+    SHIELD_CUDA(cudaMemcpyAsync(b.meta, hm, (size_t)(3 * M + R) * 4, cudaMemcpyHostToDevice, s));
+    SHIELD_CUDA(cudaMemcpyAsync(b.att, ha, att_bytes, cudaMemcpyHostToDevice, s));
+    cudaEvent_t f0 = nullptr, f1 = nullptr;
+    if (T.level >= 1) {
+        T.h2d += (3 * M + R) * 4;
+        T.tokens += M;
+        T.requests += R;
+        f0 = T.event();
+        f1 = T.event();
+        if (f0) cudaEventRecord(f0, s);
+    }
 
     const Tensor &emb = d.get("token_embd.weight");
     count_launch(d), check_launch(launch_embed(emb.w, d_ids, M, b.h, b.err, s), "embedding gather");
@@ -555,7 +625,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             SHIELD_CUDA(cudaMemcpyAsync(capture, src, (size_t)(M * width) * 4, cudaMemcpyDeviceToHost, s));
     };
     for (int l = 0; l < c.n_layers; l++) {
-        if (cancel && *cancel) {
+        if (cancel && *cancel && !capturing) {
             cudaStreamSynchronize(s);
             throw Error(SHIELD_ERR_CANCELLED, "cancelled");
         }
@@ -633,8 +703,9 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         QAct qh = qact(b, R, c.hidden);
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
         const int64_t V = c.vocab, nb = c.hidden / 32;
-        const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(R, ((int64_t)256 << 20) / (V * 4)));
-        float *dl = static_cast<float *>(d.sl.get((size_t)(chunk * V) * 4));
+        const int64_t chunk = ge ? R : std::max<int64_t>(1, std::min<int64_t>(R, ((int64_t)256 << 20) / (V * 4)));
+        float *dl = ge ? ge->d_logits : static_cast<float *>(d.sl.get((size_t)(chunk * V) * 4));
+        float *out = ge ? ge->h_logits : full_logits;
         for (int64_t r0 = 0; r0 < R; r0 += chunk) {
             QAct qc = qh;
             qc.M = std::min<int64_t>(chunk, R - r0);
@@ -644,10 +715,10 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             qc.ds = qh.ds + r0 * nb;
             qc.sums = qh.sums + r0 * nb;
             gemm(C, d, emb, qc, dl, V, EPI_STORE);
-            SHIELD_CUDA(cudaMemcpyAsync(full_logits + r0 * V, dl, (size_t)(qc.M * V) * 4, cudaMemcpyDeviceToHost, s));
+            SHIELD_CUDA(cudaMemcpyAsync(out + r0 * V, dl, (size_t)(qc.M * V) * 4, cudaMemcpyDeviceToHost, s));
             if (T.level >= 1) T.d2h += qc.M * V * 4;
         }
-        SHIELD_CUDA(cudaStreamSynchronize(s));
+        if (!ge) SHIELD_CUDA(cudaStreamSynchronize(s));
     } else if (nv > 0) {
         // last position of every request -> final norm -> verdict rows of the tied head
         const Tensor &on = d.get("output_norm.weight");
@@ -659,12 +730,31 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             T.fwd.emplace_back(f0, f1);
             f0 = f1 = nullptr;
         }
-        SHIELD_CUDA(cudaMemcpyAsync(b.h_logits, b.logits, (size_t)R * nv * 4, cudaMemcpyDeviceToHost, s));
+        SHIELD_CUDA(cudaMemcpyAsync(ge ? ge->h_logits : b.h_logits, b.logits, (size_t)R * nv * 4,
+                                    cudaMemcpyDeviceToHost, s));
         if (T.level >= 1) T.d2h += (int64_t)R * nv * 4;
     }
     if (f1 && f0) {
         cudaEventRecord(f1, s);
         T.fwd.emplace_back(f0, f1);
+    }
+    if (capturing) {
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        capturing = false;  // the guard has nothing left to undo
+        T.level = saved_level;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&ge->exec, g, 0);
+        if (g) cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            d.clear_graphs();
+            throw Error(SHIELD_ERR_CUDA, std::string("decode graph: ") + cudaGetErrorString(e));
+        }
+        SHIELD_CUDA(cudaGraphLaunch(ge->exec, s));
+        SHIELD_CUDA(cudaStreamSynchronize(s));
+        check_device_error(d);
+        if (full_logits) memcpy(full_logits, ge->h_logits, (size_t)R * c.vocab * 4);
+        else if (nv > 0) memcpy(b.h_logits, ge->h_logits, (size_t)R * nv * 4);
+        return;
     }
     check_device_error(d);
 }
@@ -1172,7 +1262,18 @@ static void seq_forward(Ctx &C, const int64_t *seq, const int32_t *ids, const in
                 for (size_t j = 0; j < B.req.size(); j++)
                     memcpy(packed.data() + B.start[j], ids + offsets[B.req[j]], (size_t)B.len[j] * 4);
                 full.resize(B.req.size() * (size_t)V);
-                forward_batch(C, d, packed.data(), B, 0, cancel, -1, 0, nullptr, full.data());
+                const bool decode_step =
+                    std::all_of(B.len.begin(), B.len.end(), [](int32_t l) { return l == 1; });
+                try {
+                    forward_batch(C, d, packed.data(), B, 0, cancel, -1, 0, nullptr, full.data(), false,
+                                  decode_step && !d.no_graphs);
+                } catch (const Error &e) {
+                    // a step that could not be captured runs as plain launches (no
+                    // GPU work ran yet; a replayed step only rewrites the same rows)
+                    if (!decode_step || d.no_graphs || e.code == SHIELD_ERR_CANCELLED) throw;
+                    d.no_graphs = true;
+                    forward_batch(C, d, packed.data(), B, 0, cancel, -1, 0, nullptr, full.data());
+                }
                 for (size_t j = 0; j < B.req.size(); j++) {
                     d.seqs.at(seq[B.req[j]]).len += B.len[j];
                     if (logits) memcpy(logits + (int64_t)B.req[j] * V, full.data() + j * V, (size_t)V * 4);
