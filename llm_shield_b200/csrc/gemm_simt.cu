@@ -204,13 +204,34 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
     float f = 0.0f;  // lane m < M: token m's output
     for (int64_t c0 = 0; c0 < nb; c0 += 32) {
         const int64_t b = c0 + lane;
+        int one_dot = 0;
+        float one_p = 0.0f, one_off = 0.0f, one_ds = 0.0f;
         if (b < nb) {
             const uint8_t *blk = row + b * block_bytes(TYPE);
             int wq[8];
             block_to_i8x4<TYPE>(blk, wq);
             const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
             if (OFF) s_off[wid][lane] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
-            for (int m = 0; m < M; m++) {
+            if (M == 1) {  // one token: the chain runs from registers (below)
+                const int4 *a4 = reinterpret_cast<const int4 *>(A + b * 32);
+                const int4 x0 = a4[0], x1 = a4[1];
+                int acc = 0;
+                acc = __dp4a(wq[0], x0.x, acc);
+                acc = __dp4a(wq[1], x0.y, acc);
+                acc = __dp4a(wq[2], x0.z, acc);
+                acc = __dp4a(wq[3], x0.w, acc);
+                acc = __dp4a(wq[4], x1.x, acc);
+                acc = __dp4a(wq[5], x1.y, acc);
+                acc = __dp4a(wq[6], x1.z, acc);
+                acc = __dp4a(wq[7], x1.w, acc);
+                one_dot = acc;
+                one_p = __fmul_rn(dw, da[b]);
+                if (OFF) {
+                    one_off = s_off[wid][lane];
+                    one_ds = ds[b];
+                }
+            }
+            for (int m = 0; M > 1 && m < M; m++) {
                 const int4 *a4 = reinterpret_cast<const int4 *>(A + (int64_t)m * K + b * 32);
                 const int4 x0 = a4[0], x1 = a4[1];
                 int acc = 0;
@@ -227,7 +248,21 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
             }
         }
         __syncwarp();
-        if (lane < M) {
+        if (M == 1) {
+            // the chunk's 32 blocks in order: every lane hands its block to lane 0
+            const int nblk = nb - c0 < 32 ? (int)(nb - c0) : 32;
+#pragma unroll
+            for (int l = 0; l < 32; l++) {
+                const int di = __shfl_sync(0xffffffffu, one_dot, l);
+                const float pi = __shfl_sync(0xffffffffu, one_p, l);
+                const float oi = OFF ? __shfl_sync(0xffffffffu, one_off, l) : 0.0f;
+                const float si = OFF ? __shfl_sync(0xffffffffu, one_ds, l) : 0.0f;
+                if (l < nblk) {
+                    f = __fmaf_rn((float)di, pi, f);
+                    if (OFF) f = __fmaf_rn(oi, si, f);
+                }
+            }
+        } else if (lane < M) {
             const int nblk = nb - c0 < 32 ? (int)(nb - c0) : 32;
             for (int l = 0; l < nblk; l++) {
                 f = __fmaf_rn((float)s_dot[wid][l][lane], s_p[wid][l][lane], f);
