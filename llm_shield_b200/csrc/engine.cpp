@@ -645,9 +645,9 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
         gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
         count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 d.temp, b.ctx, s), "rope q");
+                                 d.temp, b.ctx, s, l == capture_layer && capture_what == SHIELD_ACT_Q_ROPE), "rope q");
         count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 nullptr, b.kc, s), "rope k");
+                                 nullptr, b.kc, s, l == capture_layer && capture_what == SHIELD_ACT_K_ROPE), "rope k");
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());

@@ -67,14 +67,66 @@ __global__ void k_rope(float *__restrict__ x, int64_t M, int heads, int head_dim
     }
 }
 
+// The same rotation for the attention's layout: one warp per (token, head)
+// row of 128 dims, lane l taking dims 4l..4l+3 (pairs 2l, 2l+1; pairs from
+// `half` on are not rotated, as in Rope.Apply). The rotated row goes to perm
+// in chain-major order through a shared-memory transpose (16-byte stores),
+// and back to x in place only when natural is set.
+__global__ void __launch_bounds__(256) k_rope_rows(float *__restrict__ x, int64_t rows, int heads, int64_t ld,
+                                                   const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
+                                                   const float *__restrict__ sin_t, int half,
+                                                   const float *__restrict__ temp, float *__restrict__ perm,
+                                                   bool natural) {
+    __shared__ float srow[8][att::HD];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + wid;
+    if (row >= rows) return;  // whole warp
+    const int64_t t = row / heads;
+    const int h = (int)(row % heads);
+    const int ps = pos[t];
+    float *hd = x + t * ld + (int64_t)h * att::HD;
+    float4 v = *reinterpret_cast<const float4 *>(hd + 4 * lane);
+    float y[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int p = 2 * lane + k;
+        if (p >= half) continue;
+        const float c = cos_t[(int64_t)ps * half + p], sn = sin_t[(int64_t)ps * half + p];
+        const float x0 = y[2 * k], x1 = y[2 * k + 1];
+        float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+        if (temp) {
+            const float f = temp[ps];
+            y0 = __fmul_rn(y0, f);
+            y1 = __fmul_rn(y1, f);
+        }
+        y[2 * k] = y0;
+        y[2 * k + 1] = y1;
+    }
+    if (natural) *reinterpret_cast<float4 *>(hd + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
+#pragma unroll
+    for (int e = 0; e < 4; e++) srow[wid][chain_pos(4 * lane + e)] = y[e];
+    __syncwarp();
+    *reinterpret_cast<float4 *>(perm + t * ld + (int64_t)h * att::HD + 4 * lane) =
+        *reinterpret_cast<const float4 *>(&srow[wid][4 * lane]);
+}
+
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool natural) {
+    if (M == 0) return cudaSuccess;
+    if (perm) {
+        if (head_dim != att::HD || ld % 4 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(perm) % 16)
+            return cudaErrorInvalidValue;
+        const int64_t rows = M * heads;
+        k_rope_rows<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, rows, heads, ld, pos, cos_t, sin_t, half, temp, perm,
+                                                               natural);
+        return cudaGetLastError();
+    }
     int64_t n = M * heads * half;
     if (n == 0) return cudaSuccess;
-    if (perm && head_dim != att::HD) return cudaErrorInvalidValue;
     k_rope<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, M, heads, head_dim, ld, pos, cos_t, sin_t, half, temp,
-                                                        perm);
+                                                        nullptr);
     return cudaGetLastError();
 }
 

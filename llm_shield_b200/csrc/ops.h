@@ -82,11 +82,12 @@ cudaError_t launch_qmatmul_noalloc(const DevWeight &w, const float *x, int64_t M
                                    int32_t *err_out, cudaStream_t s);
 int64_t noalloc_max_elements();
 
-// perm (nullable): also write the rotated heads in chain-major order, the key
-// layout the attention reads (head_dim 128 only).
+// In place on x, or, with perm (head_dim 128 only), into perm in the
+// chain-major order the attention reads — and into x as well only when
+// natural is set (the rotated x is then needed only to inspect it).
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
-                        cudaStream_t s);
+                        cudaStream_t s, bool natural = true);
 // Causal GQA attention of a group of requests (three kernels, see forward_ops.cu).
 // work[i] = {request, first query token}; one CTA per (work item, KV head)
 // covers attention_rows_per_cta() query rows (tokens x the heads of a group).
