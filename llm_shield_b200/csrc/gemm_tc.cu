@@ -172,11 +172,6 @@ __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16])
         : "memory");
 }
 
-// Word of token T's scale for block j in a [BM][CHUNK] f32 tile stored by TMA
-// with 32-byte swizzling (the 16-byte halves of a 32-byte row swap when bit 2
-// of the row is set), which spreads 8 consecutive tokens over all banks.
-__device__ __forceinline__ int da_word(int T, int j) { return T * CHUNK + (j ^ (((T >> 2) & 1) << 2)); }
-
 
 // Shared-memory loads at 32-bit shared addresses (kept in order with the
 // barrier waits that publish the data).
@@ -660,7 +655,10 @@ static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t 
 }
 
 // Per-token activation scales, [M][nb] f32 -> box of CHUNK blocks x BM tokens,
-// 32-byte swizzled in shared memory (read back through da_word).
+// 32-byte swizzled in shared memory: token T's scale for block j is word
+// T * CHUNK + (j ^ 4 * bit 2 of T) (the 16-byte halves of a 32-byte row swap
+// when bit 2 of the row is set), which spreads 8 consecutive tokens over all
+// banks; the epilogue's d_lo / d_hi offsets encode it.
 static bool map_token_scales(CUtensorMap *m, const float *d, int64_t M, int64_t nb) {
     auto fn = encode_fn();
     if (!fn) return false;
