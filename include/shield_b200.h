@@ -153,6 +153,37 @@ shield_status shield_last_logits(shield_ctx *ctx, const int32_t *ids, const int6
 shield_status shield_set_prefix(shield_ctx *ctx, const int32_t *ids, int32_t n);
 
 /*
+ * The cached prefix's keys and values in the layout of KvCache.Snapshot
+ * (KvCache.cs:102-118), i.e. SystemPromptCache.State, the payload of its SHKV
+ * file (SystemPromptCache.cs:29-30,110-127): for P = the prefix's length,
+ * floats [layer][kv head][position][head_dim] of the keys after RoPE, then
+ * the values the same way, 2 * n_layers * n_kv_heads * P * head_dim floats.
+ * shield_get_prefix_state reads them from the context's first GPU;
+ * SHIELD_ERR_STATE if no prefix is cached, SHIELD_ERR_ARG if n_floats is not
+ * that count.
+ */
+shield_status shield_get_prefix_state(shield_ctx *ctx, float *state, int64_t n_floats);
+
+/* The number of token ids in the cached prefix, 0 when none
+ * (SystemPromptCache.TokenCount, SystemPromptCache.cs:35). */
+shield_status shield_prefix_length(shield_ctx *ctx, int32_t *n);
+
+/*
+ * SystemPromptCache.RestoreInto (SystemPromptCache.cs:66-74, KvCache.Restore
+ * KvCache.cs:121-136) without the prefill: copies a snapshot in the layout
+ * above to every GPU of the context as the cached prefix for ids[0..n), in
+ * place of the forward shield_set_prefix makes.  The caller vouches that the
+ * snapshot belongs to these weights and ids (the reference's fingerprint
+ * check, SystemPromptCache.cs:88-104, stays on the host).  A snapshot taken
+ * by shield_get_prefix_state, or by the reference from the same weights,
+ * restores bit-identical results.  SHIELD_ERR_ARG if n_floats does not
+ * match n (the message of KvCache.Restore), SHIELD_ERR_RANGE as for
+ * shield_set_prefix.  n = 0 drops the cache.
+ */
+shield_status shield_set_prefix_state(shield_ctx *ctx, const int32_t *ids, int32_t n, const float *state,
+                                      int64_t n_floats);
+
+/*
  * Incremental forwards on a KV cache, as MinistralModel.ForwardAsync appends
  * to its KvCache (MinistralModel.cs:179-271, KvCache.cs) — the prefill-then-
  * decode loop of Benchmark.cs:399-410.  A sequence is an empty cache for up

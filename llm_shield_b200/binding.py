@@ -54,7 +54,8 @@ class ShieldTiming(C.Structure):
 
 EXPORTS = [
     "shield_open", "shield_close", "shield_device_count", "shield_set_config", "shield_upload_tensor",
-    "shield_score_batch", "shield_last_logits", "shield_set_prefix", "shield_seq_create", "shield_seq_forward",
+    "shield_score_batch", "shield_last_logits", "shield_set_prefix", "shield_get_prefix_state", "shield_prefix_length",
+    "shield_set_prefix_state", "shield_seq_create", "shield_seq_forward",
     "shield_seq_length", "shield_seq_reset", "shield_seq_release", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
     "shield_debug_block_dots",
     "shield_set_gemm_path", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
@@ -82,6 +83,9 @@ def lib() -> C.CDLL:
         L.shield_score_batch.argtypes = [P, P, P, C.c_int32, P, C.c_int32, C.c_int32, P, P, P, P, P]
         L.shield_last_logits.argtypes = [P, P, P, C.c_int32, P, P]
         L.shield_set_prefix.argtypes = [P, P, C.c_int32]
+        L.shield_get_prefix_state.argtypes = [P, P, C.c_int64]
+        L.shield_prefix_length.argtypes = [P, C.POINTER(C.c_int32)]
+        L.shield_set_prefix_state.argtypes = [P, P, C.c_int32, P, C.c_int64]
         L.shield_seq_create.argtypes = [P, C.c_int32, C.c_int32, C.POINTER(C.c_int64)]
         L.shield_seq_forward.argtypes = [P, P, P, P, C.c_int32, P, P]
         L.shield_seq_length.argtypes = [P, C.c_int64, C.POINTER(C.c_int32)]
@@ -231,6 +235,30 @@ class ShieldContext:
         (empty: drop the cache)."""
         a = np.ascontiguousarray(ids, np.int32)
         _check(lib().shield_set_prefix(self._h, _p(a) if a.size else None, a.size))
+
+    def prefix_length(self) -> int:
+        """Token ids in the cached prefix (0: none)."""
+        n = C.c_int32()
+        _check(lib().shield_prefix_length(self._h, C.byref(n)))
+        return n.value
+
+    def get_prefix_state(self) -> np.ndarray:
+        """The cached prefix's keys and values in KvCache.Snapshot's layout
+        (KvCache.cs:102-118): [2][layer][kv head][position][head_dim] floats,
+        keys (after RoPE) first, flattened as SystemPromptCache.State."""
+        s = self.spec
+        out = np.zeros(2 * s.n_layers * s.kvdim * self.prefix_length(), np.float32)
+        _check(lib().shield_get_prefix_state(self._h, _p(out), out.size))
+        return out
+
+    def set_prefix_state(self, ids, state) -> None:
+        """Restores a snapshot (layout of get_prefix_state) as the cached
+        prefix for ids on every GPU, without forwarding it
+        (SystemPromptCache.RestoreInto, SystemPromptCache.cs:66-74)."""
+        a = np.ascontiguousarray(ids, np.int32)
+        st = np.ascontiguousarray(state, np.float32).reshape(-1)
+        _check(lib().shield_set_prefix_state(self._h, _p(a) if a.size else None, a.size,
+                                             _p(st) if st.size else None, st.size))
 
     def score_packed(self, ids: np.ndarray, offsets: np.ndarray, verdict_ids, n_yes: int, cancel=None):
         v = np.ascontiguousarray(verdict_ids, np.int32)

@@ -1169,6 +1169,92 @@ static void set_prefix(Ctx &C, const int32_t *ids, int32_t n) {
     }
 }
 
+// Floats in a snapshot of n cached positions: KvCache.Snapshot's keys for
+// every layer and kv head, then the values (KvCache.cs:102-118).
+static int64_t prefix_state_floats(const Config &c, int64_t n) { return 2 * (int64_t)c.n_layers * c.kvdim() * n; }
+
+// SystemPromptCache.RestoreInto / KvCache.Restore (SystemPromptCache.cs:66-74,
+// KvCache.cs:121-136) onto every GPU. One layer's keys (and its values) are a
+// contiguous range of the snapshot; each goes through the pinned staging
+// buffers into a device scratch that a kernel reorders into the layout the
+// attention reads. The scratch is reused layer after layer in stream order.
+static void set_prefix_state(Ctx &C, const int32_t *ids, int32_t n, const float *state, int64_t n_floats) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (n < 0 || (n > 0 && (!ids || !state))) throw Error(SHIELD_ERR_ARG, "bad prefix");
+    if (n >= C.cfg.max_positions)
+        throw Error(SHIELD_ERR_RANGE, "a prefix of " + std::to_string(n) + " tokens leaves no position below max_positions");
+    const Config &c = C.cfg;
+    const int64_t want = prefix_state_floats(c, n);
+    if (n_floats != want)
+        throw Error(SHIELD_ERR_ARG, "Snapshot holds " + std::to_string(n_floats) + " floats; " + std::to_string(n) +
+                                        " positions need " + std::to_string(want) + ".");
+    clear_prefix(C);
+    if (n == 0) return;
+    validate_ids(C, ids, n);
+    const int64_t layer = (int64_t)n * c.kvdim();  // floats of one layer's keys
+    try {
+        for_each_device(C, [&](Device &d) {
+            SHIELD_CUDA(cudaSetDevice(d.ordinal));
+            dev_alloc(d.pre_k, (size_t)(c.n_layers * layer));
+            dev_alloc(d.pre_v, (size_t)(c.n_layers * layer));
+            float *tmp = nullptr;
+            dev_alloc(tmp, (size_t)(2 * layer));
+            try {
+                for (int l = 0; l < c.n_layers; l++) {
+                    stage_to_device(d, tmp, state + l * layer, (size_t)layer * 4);
+                    stage_to_device(d, tmp + layer, state + want / 2 + l * layer, (size_t)layer * 4);
+                    check_launch(launch_prefix_state(d.pre_k + l * layer, d.pre_v + l * layer, tmp, tmp + layer, n,
+                                                     c.n_kv_heads, c.head_dim, true, d.stream),
+                                 "restore prefix state");
+                }
+                SHIELD_CUDA(cudaStreamSynchronize(d.stream));
+            } catch (...) {
+                dev_free(tmp);
+                throw;
+            }
+            dev_free(tmp);
+        });
+    } catch (...) {
+        clear_prefix(C);
+        throw;
+    }
+    C.prefix.assign(ids, ids + n);
+}
+
+// KvCache.Snapshot of the cached prefix (KvCache.cs:102-118), as
+// SystemPromptCache.CaptureAsync takes it (SystemPromptCache.cs:51-60), read
+// from the first GPU layer by layer.
+static void get_prefix_state(Ctx &C, float *state, int64_t n_floats) {
+    if (!C.configured) throw Error(SHIELD_ERR_STATE, "no model configured");
+    if (C.prefix.empty()) throw Error(SHIELD_ERR_STATE, "no prefix is cached");
+    const Config &c = C.cfg;
+    const int64_t n = (int64_t)C.prefix.size();
+    const int64_t want = prefix_state_floats(c, n);
+    if (!state || n_floats != want)
+        throw Error(SHIELD_ERR_ARG, "the snapshot of " + std::to_string(n) + " positions holds " +
+                                        std::to_string(want) + " floats; the buffer has " + std::to_string(n_floats) + ".");
+    Device &d = *C.devs[0];
+    SHIELD_CUDA(cudaSetDevice(d.ordinal));
+    const int64_t layer = n * c.kvdim();
+    float *tmp = nullptr;
+    dev_alloc(tmp, (size_t)(2 * layer));
+    try {
+        for (int l = 0; l < c.n_layers; l++) {
+            check_launch(launch_prefix_state(d.pre_k + l * layer, d.pre_v + l * layer, tmp, tmp + layer, n,
+                                             c.n_kv_heads, c.head_dim, false, d.stream),
+                         "read prefix state");
+            SHIELD_CUDA(cudaMemcpyAsync(state + l * layer, tmp, (size_t)layer * 4, cudaMemcpyDeviceToHost, d.stream));
+            SHIELD_CUDA(cudaMemcpyAsync(state + want / 2 + l * layer, tmp + layer, (size_t)layer * 4,
+                                        cudaMemcpyDeviceToHost, d.stream));
+        }
+        SHIELD_CUDA(cudaStreamSynchronize(d.stream));
+    } catch (...) {
+        dev_free(tmp);
+        throw;
+    }
+    dev_free(tmp);
+}
+
 // ---------------------------------------------------------- sequences
 
 static Device &device_of(Ctx &C, int32_t device);
@@ -1491,6 +1577,28 @@ shield_status shield_set_prefix(shield_ctx *ctx, const int32_t *ids, int32_t n) 
     return guarded([&] {
         if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
         set_prefix(ctx->c, ids, n);
+    });
+}
+
+shield_status shield_get_prefix_state(shield_ctx *ctx, float *state, int64_t n_floats) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        get_prefix_state(ctx->c, state, n_floats);
+    });
+}
+
+shield_status shield_prefix_length(shield_ctx *ctx, int32_t *n) {
+    return guarded([&] {
+        if (!ctx || !n) throw Error(SHIELD_ERR_ARG, "ctx or n is null");
+        *n = (int32_t)ctx->c.prefix.size();
+    });
+}
+
+shield_status shield_set_prefix_state(shield_ctx *ctx, const int32_t *ids, int32_t n, const float *state,
+                                      int64_t n_floats) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        set_prefix_state(ctx->c, ids, n, state, n_floats);
     });
 }
 

@@ -453,4 +453,35 @@ cudaError_t launch_append_kv(const AttArgs &A, const uint8_t *append, int n_req,
     return cudaGetLastError();
 }
 
+// One thread per (position, head, stored dim c) of the device layout. Chain
+// position c holds dim 4·(c % 32) + c / 32 (the inverse of chain_pos), so the
+// snapshot's natural-order key row is read through that map; values are
+// stored in natural order on both sides.
+__global__ void k_prefix_state(float *__restrict__ dev_k, float *__restrict__ dev_v, float *__restrict__ snap_k,
+                               float *__restrict__ snap_v, int64_t P, int kv_heads, bool to_device) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= P * kv_heads * att::HD) return;
+    const int c = (int)(i % att::HD);
+    const int h = (int)((i / att::HD) % kv_heads);
+    const int64_t pos = i / ((int64_t)kv_heads * att::HD);
+    const int64_t row = ((int64_t)h * P + pos) * att::HD;
+    const int d = 4 * (c & 31) + (c >> 5);
+    if (to_device) {
+        dev_k[i] = snap_k[row + d];
+        dev_v[i] = snap_v[row + c];
+    } else {
+        snap_k[row + d] = dev_k[i];
+        snap_v[row + c] = dev_v[i];
+    }
+}
+
+cudaError_t launch_prefix_state(float *dev_k, float *dev_v, float *snap_k, float *snap_v, int64_t P, int kv_heads,
+                                int head_dim, bool to_device, cudaStream_t s) {
+    if (head_dim != att::HD || kv_heads <= 0 || P < 0) return cudaErrorInvalidValue;
+    const int64_t n = P * kv_heads * att::HD;
+    if (n == 0) return cudaSuccess;
+    k_prefix_state<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev_k, dev_v, snap_k, snap_v, P, kv_heads, to_device);
+    return cudaGetLastError();
+}
+
 }  // namespace shield

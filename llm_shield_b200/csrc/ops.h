@@ -116,6 +116,12 @@ cudaError_t launch_attention(const AttArgs &args, int n_work, int head_dim, cuda
 // to position req_pre[r] + t of that cache (KvCache.Append, KvCache.cs).
 cudaError_t launch_append_kv(const AttArgs &args, const uint8_t *append, int n_req, int64_t M, int kvdim,
                              cudaStream_t s);
+// One layer of cached keys and values between the device layout ([position]
+// [kv head][head_dim], keys chain-major) and KvCache.Snapshot's ([kv head]
+// [position][head_dim], natural order; KvCache.cs:102-118), for P positions.
+// to_device: snap_k/snap_v -> dev_k/dev_v; else the reverse.
+cudaError_t launch_prefix_state(float *dev_k, float *dev_v, float *snap_k, float *snap_v, int64_t P, int kv_heads,
+                                int head_dim, bool to_device, cudaStream_t s);
 int attention_rows_per_cta();
 // Scores of one (head, query) row are stored with a row stride rounded up to
 // 4 floats, so that every row starts on a 16-byte boundary.

@@ -51,7 +51,15 @@ def test_prefix_cache_on_both_gpus(two):
     both.set_prefix(prefix)
     try:
         np.testing.assert_array_equal(both.score_batch(reqs, spec.verdict_ids, len(spec.yes_ids))[3], ref)
+        # a snapshot taken on one GPU, restored onto both without a prefill
+        one.set_prefix(prefix)
+        state = one.get_prefix_state()
+        np.testing.assert_array_equal(both.get_prefix_state(), state)
+        both.set_prefix([])
+        both.set_prefix_state(prefix, state)
+        np.testing.assert_array_equal(both.score_batch(reqs, spec.verdict_ids, len(spec.yes_ids))[3], ref)
     finally:
+        one.set_prefix([])
         both.set_prefix([])
 
 

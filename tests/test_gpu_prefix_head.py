@@ -11,7 +11,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from llm_shield_b200 import binding, synth
+import oracle
+from llm_shield_b200 import binding, prefix_file, synth
 from helpers import oracle_model
 
 pytestmark = pytest.mark.gpu
@@ -103,5 +104,69 @@ def test_full_head_matches_the_verdict_rows_and_the_oracle(model):
     ctx.set_prefix(prefix)
     try:
         np.testing.assert_array_equal(ctx.last_logits(reqs), full)
+    finally:
+        ctx.set_prefix([])
+
+
+def _oracle_snapshot(spec, tensors, prefix):
+    """KvCache.Snapshot (KvCache.cs:102-118) of the oracle's forward of the
+    prefix: per layer its keys after RoPE and its values, [kv head][position]
+    [head_dim], keys of every layer first."""
+    om = oracle_model(spec, tensors)
+    parts = {oracle.CAP_K_ROPE: [], oracle.CAP_V: []}
+    for what in parts:
+        for layer in range(spec.n_layers):
+            _, cap = om.forward(prefix, np.array([0], np.int32), capture_layer=layer, capture_what=what)
+            parts[what].append(cap.reshape(prefix.size, spec.n_kv_heads, spec.head_dim).transpose(1, 0, 2).ravel())
+    return np.concatenate(parts[oracle.CAP_K_ROPE] + parts[oracle.CAP_V])
+
+
+def test_prefix_state_is_the_oracle_snapshot_and_restores_bit_identically(model):
+    spec, tensors, ctx = model
+    prefix = np.random.default_rng(12).integers(1, spec.vocab, size=34, dtype=np.int32)
+    reqs = _requests(spec, prefix)
+    args = (spec.verdict_ids, len(spec.yes_ids))
+    ref = ctx.score_batch(reqs, *args)[3]
+    ctx.set_prefix(prefix)
+    try:
+        assert ctx.prefix_length() == prefix.size
+        state = ctx.get_prefix_state()
+        np.testing.assert_array_equal(state, _oracle_snapshot(spec, tensors, prefix))
+        ctx.set_prefix([])
+        assert ctx.prefix_length() == 0
+        with pytest.raises(binding.ShieldError) as e:
+            ctx.get_prefix_state()
+        assert e.value.code == binding.ERR_STATE
+        ctx.set_prefix_state(prefix, state)  # no prefill: the snapshot goes to the GPU as it is
+        assert ctx.prefix_length() == prefix.size
+        np.testing.assert_array_equal(ctx.score_batch(reqs, *args)[3], ref)
+        np.testing.assert_array_equal(ctx.get_prefix_state(), state)
+        with pytest.raises(binding.ShieldError) as e:  # KvCache.Restore's size check
+            ctx.set_prefix_state(prefix[:-1], state)
+        assert e.value.code == binding.ERR_ARG
+        assert ctx.prefix_length() == prefix.size  # a rejected snapshot leaves the cache alone
+        with pytest.raises(binding.ShieldError) as e:
+            ctx.set_prefix_state(np.full(34, spec.vocab, np.int32), state)
+        assert e.value.code == binding.ERR_RANGE
+    finally:
+        ctx.set_prefix([])
+
+
+def test_snapshot_file_skips_the_prefill(model, tmp_path):
+    spec, _, ctx = model
+    weights = tmp_path / "model.gguf"
+    weights.write_bytes(b"synthetic")
+    ident = prefix_file.ModelIdentity(str(weights), "mistral3", spec.n_layers, spec.n_kv_heads, spec.head_dim)
+    prefix = np.random.default_rng(13).integers(1, spec.vocab, size=20, dtype=np.int32)
+    reqs = _requests(spec, prefix)
+    args = (spec.verdict_ids, len(spec.yes_ids))
+    ref = ctx.score_batch(reqs, *args)[3]
+    path = tmp_path / "prefix.shkv"
+    try:
+        captured = prefix_file.load_or_capture(ctx, ident, prefix, path)
+        ctx.set_prefix([])
+        restored = prefix_file.load_or_capture(ctx, ident, prefix, path)
+        np.testing.assert_array_equal(restored.state, captured.state)
+        np.testing.assert_array_equal(ctx.score_batch(reqs, *args)[3], ref)
     finally:
         ctx.set_prefix([])
