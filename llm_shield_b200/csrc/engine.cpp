@@ -1141,9 +1141,9 @@ static void set_prefix(Ctx &C, const int32_t *ids, int32_t n) {
     if (n < 0 || (n > 0 && !ids)) throw Error(SHIELD_ERR_ARG, "bad prefix");
     if (n >= C.cfg.max_positions)
         throw Error(SHIELD_ERR_RANGE, "a prefix of " + std::to_string(n) + " tokens leaves no position below max_positions");
+    validate_ids(C, ids, n);  // a rejected prefix leaves the cached one in place
     clear_prefix(C);
     if (n == 0) return;
-    validate_ids(C, ids, n);
     const Config &c = C.cfg;
     for (auto &dp : C.devs) {
         Device &d = *dp;
@@ -1188,9 +1188,9 @@ static void set_prefix_state(Ctx &C, const int32_t *ids, int32_t n, const float 
     if (n_floats != want)
         throw Error(SHIELD_ERR_ARG, "Snapshot holds " + std::to_string(n_floats) + " floats; " + std::to_string(n) +
                                         " positions need " + std::to_string(want) + ".");
+    validate_ids(C, ids, n);
     clear_prefix(C);
     if (n == 0) return;
-    validate_ids(C, ids, n);
     const int64_t layer = (int64_t)n * c.kvdim();  // floats of one layer's keys
     try {
         for_each_device(C, [&](Device &d) {

@@ -148,6 +148,7 @@ def test_prefix_state_is_the_oracle_snapshot_and_restores_bit_identically(model)
         with pytest.raises(binding.ShieldError) as e:
             ctx.set_prefix_state(np.full(34, spec.vocab, np.int32), state)
         assert e.value.code == binding.ERR_RANGE
+        np.testing.assert_array_equal(ctx.get_prefix_state(), state)
     finally:
         ctx.set_prefix([])
 
