@@ -32,7 +32,7 @@ def two(shield_lib):
 
 def test_scores_and_full_head_do_not_depend_on_the_gpu_count(two):
     spec, (one, both) = two
-    assert both.device_count() == 2
+    assert both.device_count == 2
     lengths = [3, 200, 17, 64, 1, 120, 45, 9, 300, 33, 77, 2]
     reqs = synth.random_requests(len(lengths), lengths, seed=4, vocab=spec.vocab)
     a = one.score_batch(reqs, spec.verdict_ids, len(spec.yes_ids))
