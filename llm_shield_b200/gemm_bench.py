@@ -7,6 +7,12 @@ pre-unpacked copy apply), then times `shield_qmatmul_device` on device-resident
 f32 activations: the whole call (activation quantization + GEMM) with CUDA
 events on the library's stream, and the GEMM launches alone with the library's
 level-2 timing. Prints one JSON line per GEMM path.
+
+    python -m llm_shield_b200.gemm_bench --int8-peak
+
+instead measures the dense int8 tensor-core rate the roofline compares
+against: cuBLASLt through `torch._int_mm` on square int8 operands, best of
+`--reps` per size, 2·n^3 ops per call.
 """
 from __future__ import annotations
 
@@ -18,6 +24,29 @@ from . import binding, synth
 PATHS = {"auto": 0, "simt": 1, "raw": 2, "pre": 3}
 
 
+def int8_peak(sizes=(8192, 16384), reps: int = 10, warmup: int = 3) -> None:
+    import torch
+
+    for n in sizes:
+        g = torch.Generator(device="cuda").manual_seed(n)
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g).t()  # column-major
+        for _ in range(warmup):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(reps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        print(json.dumps({"int8_dense": "torch._int_mm", "n": n, "best_ms": round(best, 4),
+                          "tops": round(2.0 * n ** 3 / best / 1e9, 1), "nominal_tops": 4500}), flush=True)
+        del a, b
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--type", default="Q4_0", choices=[synth.TYPE_NAMES[t] for t in synth.BLOCK_BYTES])
@@ -27,7 +56,11 @@ def main(argv=None) -> None:
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--paths", default="pre", help="comma list of auto, simt, raw, pre")
+    ap.add_argument("--int8-peak", action="store_true", help="measure the dense int8 rate instead")
     args = ap.parse_args(argv)
+    if args.int8_peak:
+        int8_peak(reps=args.reps, warmup=args.warmup)
+        return
 
     import torch
 
