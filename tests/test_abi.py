@@ -57,3 +57,40 @@ def test_open_without_a_gpu_fails_loudly():
     rc = binding.lib().shield_open(1, ctypes.byref(h))
     assert rc == binding.ERR_CUDA
     assert b"cuda" in binding.lib().shield_last_error().lower()
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "shield_b200.h"
+
+int main(void) {
+    shield_ctx *ctx = NULL;
+    shield_status rc = shield_open(1, &ctx);
+    const char *msg = shield_last_error();
+    if (rc == SHIELD_OK) { shield_close(ctx); return 0; }   /* a GPU is present */
+    if (rc != SHIELD_ERR_CUDA || ctx != NULL || msg == NULL || strlen(msg) == 0) return 1;
+    if (shield_set_prefix(NULL, NULL, 0) != SHIELD_ERR_ARG) return 2;
+    if (shield_prefix_length(NULL, NULL) != SHIELD_ERR_ARG) return 3;
+    printf("%d\n", rc);
+    return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_links_from_c(tmp_path):
+    """What a cgo, P/Invoke or ctypes consumer sees: the header compiles as
+    strict C99 and a C program links against the library and gets status
+    codes back (no GPU here, so shield_open reports a CUDA failure)."""
+    src = tmp_path / "client.c"
+    src.write_text(C_CLIENT)
+    lib = _build.build_main()
+    exe = tmp_path / "client"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", str(REPO / "include"),
+                    str(src), "-o", str(exe), "-L", str(lib.parent), "-l:" + lib.name,
+                    "-Wl,-rpath," + str(lib.parent)], check=True)
+    import torch
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    if not torch.cuda.is_available():
+        assert r.stdout.strip() == str(binding.ERR_CUDA)
