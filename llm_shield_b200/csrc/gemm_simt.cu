@@ -145,12 +145,12 @@ cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t
 
 // ---------------------------------------------------------------- few tokens
 //
-// A handful of tokens (decode steps, the last rows of a batch): one warp per
-// output row, so every weight byte is read once and the whole GPU works on one
-// launch. Lane l takes blocks l, l+32, .. of a 32-block chunk: it unpacks the
-// block to signed int8 weights, forms each token's exact dot with dp4a and the
-// scale product dw·da; the chunk's results go through shared memory so that
-// lane m then runs token m's chain over the chunk in block order,
+// A handful of tokens (decode steps, the last rows of a batch): every weight
+// byte is read once and the whole GPU works on one launch. The per-block work
+// (unpack a block to signed int8 weights, each token's exact dot with dp4a,
+// the scale product dw·da) runs in parallel over blocks; the results go
+// through shared memory so that one thread per output then runs its chain in
+// block order,
 //   f = fma(float(i), dw·da, f)   (then f = fma(m_w, d_a·Σa, f) for Q4_1/Q5_1)
 // the same operations, in the same order, as every other GEMM here.
 constexpr int GEMV_WARPS = 4;
@@ -187,6 +187,11 @@ __device__ __forceinline__ void block_to_i8x4(const uint8_t *blk, int (&wq)[8]) 
     }
 }
 
+// 2..16 tokens: one warp per output row. Per chunk of 32 blocks each lane
+// unpacks one block and forms its dp4a dots and scale products for every
+// token into shared memory; then lane m runs token m's chain over the chunk
+// in block order, f = fma(float(dot), dw·da, f) (+ fma(m, Σa·da, f)), the
+// reference's order (IntegerGemm.cs:371-457).
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
 k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
@@ -204,34 +209,13 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
     float f = 0.0f;  // lane m < M: token m's output
     for (int64_t c0 = 0; c0 < nb; c0 += 32) {
         const int64_t b = c0 + lane;
-        int one_dot = 0;
-        float one_p = 0.0f, one_off = 0.0f, one_ds = 0.0f;
         if (b < nb) {
             const uint8_t *blk = row + b * block_bytes(TYPE);
             int wq[8];
             block_to_i8x4<TYPE>(blk, wq);
             const float dw = h2f(*reinterpret_cast<const uint16_t *>(blk));
             if (OFF) s_off[wid][lane] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
-            if (M == 1) {  // one token: the chain runs from registers (below)
-                const int4 *a4 = reinterpret_cast<const int4 *>(A + b * 32);
-                const int4 x0 = a4[0], x1 = a4[1];
-                int acc = 0;
-                acc = __dp4a(wq[0], x0.x, acc);
-                acc = __dp4a(wq[1], x0.y, acc);
-                acc = __dp4a(wq[2], x0.z, acc);
-                acc = __dp4a(wq[3], x0.w, acc);
-                acc = __dp4a(wq[4], x1.x, acc);
-                acc = __dp4a(wq[5], x1.y, acc);
-                acc = __dp4a(wq[6], x1.z, acc);
-                acc = __dp4a(wq[7], x1.w, acc);
-                one_dot = acc;
-                one_p = __fmul_rn(dw, da[b]);
-                if (OFF) {
-                    one_off = s_off[wid][lane];
-                    one_ds = ds[b];
-                }
-            }
-            for (int m = 0; M > 1 && m < M; m++) {
+            for (int m = 0; m < M; m++) {
                 const int4 *a4 = reinterpret_cast<const int4 *>(A + (int64_t)m * K + b * 32);
                 const int4 x0 = a4[0], x1 = a4[1];
                 int acc = 0;
@@ -248,21 +232,7 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
             }
         }
         __syncwarp();
-        if (M == 1) {
-            // the chunk's 32 blocks in order: every lane hands its block to lane 0
-            const int nblk = nb - c0 < 32 ? (int)(nb - c0) : 32;
-#pragma unroll
-            for (int l = 0; l < 32; l++) {
-                const int di = __shfl_sync(0xffffffffu, one_dot, l);
-                const float pi = __shfl_sync(0xffffffffu, one_p, l);
-                const float oi = OFF ? __shfl_sync(0xffffffffu, one_off, l) : 0.0f;
-                const float si = OFF ? __shfl_sync(0xffffffffu, one_ds, l) : 0.0f;
-                if (l < nblk) {
-                    f = __fmaf_rn((float)di, pi, f);
-                    if (OFF) f = __fmaf_rn(oi, si, f);
-                }
-            }
-        } else if (lane < M) {
+        if (lane < M) {
             const int nblk = nb - c0 < 32 ? (int)(nb - c0) : 32;
             for (int l = 0; l < nblk; l++) {
                 f = __fmaf_rn((float)s_dot[wid][l][lane], s_p[wid][l][lane], f);
@@ -277,8 +247,86 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
     }
 }
 
+// One token (a decode step at batch 1, the M = 1 sweep shape): GEMV1_ROWS
+// rows per CTA, their blocks in chunks of GEMV1_CHUNK. Phase 1: every thread
+// forms (row, block) dots and scale products, GEMV1_UNROLL pairs at a time so
+// their loads are in flight together; consecutive threads take consecutive
+// blocks of a row. Phase 2: thread r runs row r's chain over the chunk in
+// block order from shared memory, the same fma sequence as k_gemv_small.
+constexpr int GEMV1_ROWS = 16, GEMV1_THREADS = 256, GEMV1_CHUNK = 96, GEMV1_UNROLL = 2;
+
+template <int TYPE, int EPI>
+__global__ void __launch_bounds__(GEMV1_THREADS)
+k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
+           const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds,
+           float *__restrict__ y) {
+    constexpr bool OFF = has_offset(TYPE);
+    constexpr int LD = GEMV1_CHUNK + 1;  // odd row stride: phase 2's threads read distinct banks
+    __shared__ int32_t s_dot[GEMV1_ROWS * LD];
+    __shared__ float s_p[GEMV1_ROWS * LD];
+    __shared__ float s_m[OFF ? GEMV1_ROWS * LD : 1];
+    const int64_t n0 = (int64_t)blockIdx.x * GEMV1_ROWS;
+    const int nrow = rows - n0 < GEMV1_ROWS ? (int)(rows - n0) : GEMV1_ROWS;
+    const int64_t nb = K / 32;
+    float f = 0.0f;  // thread r < nrow: row n0 + r
+    for (int64_t c0 = 0; c0 < nb; c0 += GEMV1_CHUNK) {
+        const int nc = nb - c0 < GEMV1_CHUNK ? (int)(nb - c0) : GEMV1_CHUNK;
+        const int pairs = nrow * nc;
+        for (int base = threadIdx.x; base < pairs; base += GEMV1_THREADS * GEMV1_UNROLL) {
+#pragma unroll
+            for (int u = 0; u < GEMV1_UNROLL; u++) {
+                const int i = base + u * GEMV1_THREADS;
+                if (i < pairs) {
+                    const int r = i / nc, bl = i - r * nc;
+                    const int64_t b = c0 + bl;
+                    const uint8_t *blk = W + (n0 + r) * row_bytes + b * block_bytes(TYPE);
+                    int wq[8];
+                    block_to_i8x4<TYPE>(blk, wq);
+                    const int4 *a4 = reinterpret_cast<const int4 *>(A + b * 32);
+                    const int4 x0 = a4[0], x1 = a4[1];
+                    int acc = 0;
+                    acc = __dp4a(wq[0], x0.x, acc);
+                    acc = __dp4a(wq[1], x0.y, acc);
+                    acc = __dp4a(wq[2], x0.z, acc);
+                    acc = __dp4a(wq[3], x0.w, acc);
+                    acc = __dp4a(wq[4], x1.x, acc);
+                    acc = __dp4a(wq[5], x1.y, acc);
+                    acc = __dp4a(wq[6], x1.z, acc);
+                    acc = __dp4a(wq[7], x1.w, acc);
+                    s_dot[r * LD + bl] = acc;
+                    s_p[r * LD + bl] = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(blk)), da[b]);
+                    if (OFF) s_m[r * LD + bl] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                }
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < nrow) {
+            const int r = threadIdx.x;
+            for (int bl = 0; bl < nc; bl++) {
+                f = __fmaf_rn((float)s_dot[r * LD + bl], s_p[r * LD + bl], f);
+                if (OFF) f = __fmaf_rn(s_m[r * LD + bl], ds[c0 + bl], f);
+            }
+        }
+        __syncthreads();  // the next chunk overwrites the arrays
+    }
+    if (threadIdx.x < nrow) {
+        float *dst = y + n0 + threadIdx.x;
+        *dst = EPI == EPI_ADD ? __fadd_rn(*dst, f) : f;
+    }
+}
+
 template <int TYPE>
 static void gemv_small_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s) {
+    if (q.M == 1) {
+        const unsigned g1 = (unsigned)((w.rows + GEMV1_ROWS - 1) / GEMV1_ROWS);
+        if (epi == EPI_ADD)
+            k_gemv_one<TYPE, EPI_ADD><<<g1, GEMV1_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.da,
+                                                                   q.ds, y);
+        else
+            k_gemv_one<TYPE, EPI_STORE><<<g1, GEMV1_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8,
+                                                                     q.da, q.ds, y);
+        return;
+    }
     const unsigned grid = (unsigned)((w.rows + GEMV_WARPS - 1) / GEMV_WARPS);
     if (epi == EPI_ADD)
         k_gemv_small<TYPE, EPI_ADD><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.da,

@@ -69,9 +69,11 @@ def test_outputs_bit_identical_to_oracle(ctx, qtype, rows, cols, tokens, path):
 
 
 @pytest.mark.parametrize("qtype", INT_TYPES)
-@pytest.mark.parametrize("rows,cols", [(100, 256), (256, 3072), (3072, 9216)])
+@pytest.mark.parametrize("rows,cols", [(100, 256), (256, 3072), (3072, 9216), (37, 3200)])
 def test_few_token_kernel_bit_identical_to_oracle(ctx, qtype, rows, cols):
-    """Path 4, the one-warp-per-row kernel automatic below 17 tokens."""
+    """Path 4, the few-token kernels automatic below 17 tokens (one token: 16
+    rows per CTA in 96-block chunks, so 37 x 3200 ends in a partial CTA and a
+    partial chunk)."""
     w = random_weights(qtype, rows, cols, seed=3 * rows + qtype)
     upload(ctx, "blk.0.attn_v.weight", qtype, rows, cols, w)
     ctx.set_gemm_path(4)
