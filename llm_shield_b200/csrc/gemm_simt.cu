@@ -192,6 +192,86 @@ __device__ __forceinline__ void block_to_i8x4(const uint8_t *blk, int (&wq)[8]) 
 // token into shared memory; then lane m runs token m's chain over the chunk
 // in block order, f = fma(float(dot), dw·da, f) (+ fma(m, Σa·da, f)), the
 // reference's order (IntegerGemm.cs:371-457).
+// A whole block as 32-bit words (w[j] = block bytes 4j..4j+3), read with
+// 8-byte loads from the 8-byte boundary at or below it: blocks are only
+// 2-byte aligned, and three 8-byte loads of a Q4_0 block touch a third of the
+// cache sectors nine 2-byte loads do. The loads end at most 13 bytes past the
+// block, inside the 64 bytes of slack every uploaded weight buffer carries.
+template <int TYPE>
+struct BlockWords {
+    static constexpr int BB = block_bytes(TYPE);
+    static constexpr int NW = (BB + 3) / 4;      // words of the block
+    static constexpr int NL = (BB + 6 + 7) / 8;  // 8-byte loads that cover it at any even misalignment
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_block_words(const uint8_t *blk, uint32_t (&w)[BlockWords<TYPE>::NW]) {
+    using B = BlockWords<TYPE>;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(blk);
+    const uint2 *p = reinterpret_cast<const uint2 *>(addr & ~uintptr_t(7));
+    const uint32_t sh = (uint32_t)(addr & 7);  // 0, 2, 4 or 6
+    uint32_t raw[2 * B::NL + 2];
+#pragma unroll
+    for (int i = 0; i < B::NL; i++) {
+        const uint2 v = __ldg(p + i);
+        raw[2 * i] = v.x;
+        raw[2 * i + 1] = v.y;
+    }
+    raw[2 * B::NL] = 0u;  // only ever shifted in beyond the block's last byte
+    raw[2 * B::NL + 1] = 0u;
+    const bool skip = sh >= 4;
+    const uint32_t bits = (sh & 3u) * 8u;
+#pragma unroll
+    for (int j = 0; j < B::NW; j++) {
+        const uint32_t lo = skip ? raw[j + 1] : raw[j];
+        const uint32_t hi = skip ? raw[j + 2] : raw[j + 1];
+        w[j] = __funnelshift_r(lo, hi, bits);
+    }
+}
+
+// The 4 bytes of a block at even byte offset OFF, from its words.
+template <int OFF, int N>
+__device__ __forceinline__ uint32_t word_at(const uint32_t (&w)[N]) {
+    static_assert(OFF % 2 == 0 && OFF / 4 < N, "offset outside the block");
+    if constexpr (OFF % 4 == 0) return w[OFF / 4];
+    else return __funnelshift_r(w[OFF / 4], w[OFF / 4 + 1], 16);
+}
+
+// block_to_i8x4 from the block's words; also the f16 scale (and offset).
+template <int TYPE>
+__device__ __forceinline__ void words_to_i8x4(const uint32_t (&w)[BlockWords<TYPE>::NW], int (&wq)[8], float &dw,
+                                              float &mw) {
+    constexpr int QS = qs_offset(TYPE);
+    dw = h2f((uint16_t)(w[0] & 0xFFFFu));
+    mw = has_offset(TYPE) ? h2f((uint16_t)(w[0] >> 16)) : 0.0f;
+    if constexpr (TYPE == T_Q8_0) {
+        wq[0] = (int)word_at<QS + 0>(w);
+        wq[1] = (int)word_at<QS + 4>(w);
+        wq[2] = (int)word_at<QS + 8>(w);
+        wq[3] = (int)word_at<QS + 12>(w);
+        wq[4] = (int)word_at<QS + 16>(w);
+        wq[5] = (int)word_at<QS + 20>(w);
+        wq[6] = (int)word_at<QS + 24>(w);
+        wq[7] = (int)word_at<QS + 28>(w);
+        return;
+    } else {
+        uint32_t qh = 0;
+        if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) qh = word_at<qh_offset(TYPE)>(w);
+        const uint32_t z = (uint32_t)zero_point(TYPE) * 0x01010101u;
+        const uint32_t q[4] = {word_at<QS>(w), word_at<QS + 4>(w), word_at<QS + 8>(w), word_at<QS + 12>(w)};
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            uint32_t lo = q[g] & 0x0F0F0F0Fu, hi = (q[g] >> 4) & 0x0F0F0F0Fu;  // elements 4g.. and 16+4g..
+            if (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
+                lo |= spread4_bits((qh >> (4 * g)) & 0xFu);
+                hi |= spread4_bits((qh >> (16 + 4 * g)) & 0xFu);
+            }
+            wq[g] = (int)__vsub4(lo, z);
+            wq[4 + g] = (int)__vsub4(hi, z);
+        }
+    }
+}
+
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
 k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
@@ -279,9 +359,11 @@ k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64
                 if (i < pairs) {
                     const int r = i / nc, bl = i - r * nc;
                     const int64_t b = c0 + bl;
-                    const uint8_t *blk = W + (n0 + r) * row_bytes + b * block_bytes(TYPE);
+                    uint32_t bw[BlockWords<TYPE>::NW];
+                    load_block_words<TYPE>(W + (n0 + r) * row_bytes + b * block_bytes(TYPE), bw);
                     int wq[8];
-                    block_to_i8x4<TYPE>(blk, wq);
+                    float dw, mw;
+                    words_to_i8x4<TYPE>(bw, wq, dw, mw);
                     const int4 *a4 = reinterpret_cast<const int4 *>(A + b * 32);
                     const int4 x0 = a4[0], x1 = a4[1];
                     int acc = 0;
@@ -294,8 +376,8 @@ k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64
                     acc = __dp4a(wq[6], x1.z, acc);
                     acc = __dp4a(wq[7], x1.w, acc);
                     s_dot[r * LD + bl] = acc;
-                    s_p[r * LD + bl] = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(blk)), da[b]);
-                    if (OFF) s_m[r * LD + bl] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                    s_p[r * LD + bl] = __fmul_rn(dw, da[b]);
+                    if (OFF) s_m[r * LD + bl] = mw;
                 }
             }
         }
