@@ -262,7 +262,7 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
  * batches reading a once-unpacked f16 copy of the layer weights, short ones
  * unpacking the GGUF blocks on the fly), 1 = CUDA-core tiled kernel only,
  * 2 = tensor cores unpacking GGUF blocks only, 3 = tensor cores on the
- * unpacked copy only, 4 = the one-warp-per-row kernel only. 2, 3 and 4 fail
+ * unpacked copy only, 4 = the few-token kernels only. 2, 3 and 4 fail
  * with SHIELD_ERR_UNSUPPORTED on shapes their kernel does not take; the
  * raw/unpacked choice is process-wide. For cross-checking the kernels against
  * each other. */

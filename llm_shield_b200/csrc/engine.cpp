@@ -340,7 +340,7 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
         if (e0) cudaEventRecord(e0, d.stream);
     }
     bool done = false;
-    // 1..16 tokens: one warp per output row (decode steps, the last rows)
+    // 1..16 tokens: the few-token kernels (decode steps, the last rows)
     if ((C.gemm_path == 0 || C.gemm_path == 4) && gemv_small_supports(W.w, q.M)) {
         cudaError_t e = launch_gemv_small(W.w, q, y, ldy, epi, d.stream);
         if (e == cudaSuccess)

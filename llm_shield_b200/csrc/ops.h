@@ -61,7 +61,8 @@ cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s);
 cudaError_t launch_unpack_f16(const DevWeight &w, cudaStream_t s);
 
 // Exact integer GEMM on CUDA cores; any K % 32 == 0, optional row subset.
-// A few tokens (1..16): one warp per output row, same arithmetic as the other GEMMs.
+// A few tokens (1..16): one token 16 rows per CTA, 2..16 one warp per output
+// row; the same arithmetic as the other GEMMs.
 bool gemv_small_supports(const DevWeight &w, int64_t M);
 cudaError_t launch_gemv_small(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s);
 cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
