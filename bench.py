@@ -157,6 +157,27 @@ def gemm_traffic():
     return json.loads(p.read_text()).get("dram_bytes_per_launch")
 
 
+def host_cpu() -> dict:
+    """The host the CPU numbers ran on: model name, logical cores, the SIMD
+    flags the reference's integer GEMM chooses between (IntegerGemm.cs:58-65)
+    and the tier the oracle picked from them."""
+    import oracle
+    model, flags = "unknown", set()
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name") and model == "unknown":
+                    model = line.split(":", 1)[1].strip()
+                elif line.startswith("flags") and not flags:
+                    flags = set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    tier = {3: "AVX-VNNI", 2: "AVX512-VNNI", 1: "AVX2", 0: "scalar"}.get(oracle.lib().orc_simd_level(), "unknown")
+    return {"model": model, "nproc": os.cpu_count(),
+            "isa": sorted(flags & {"avx2", "fma", "avx_vnni", "avx512f", "avx512_vnni"}),
+            "oracle_gemm_tier": tier}
+
+
 def cpu_baseline(spec, tensors, ids, offsets, budget_s: float = 20.0):
     """The oracle (C restatement of the reference CPU path) on the host cores,
     on the first requests of the same set, until about budget_s of work."""
@@ -176,7 +197,8 @@ def cpu_baseline(spec, tensors, ids, offsets, budget_s: float = 20.0):
     dt = time.perf_counter() - t0
     return {"value": tokens / dt, "unit": "tokens/s", "verdicts_per_s": reqs / dt, "cores": threads,
             "kind": "port", "sample": f"first {reqs} requests of the config-5 set ({tokens} tokens), "
-                                     f"oracle/ C restatement of the reference CPU integer path, {dt:.1f} s"}
+                                     f"oracle/ C restatement of the reference CPU integer path, {dt:.1f} s",
+            "host": host_cpu()}
 
 
 def run_reference(args):
@@ -215,7 +237,7 @@ def run_reference(args):
                    "model": "Shieldstral-shaped 3B (26L, d3072, 32/8x128, ffn 9216, vocab 131072)"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{len(times)} requests ({total_tok} tokens), C restatement of the "
-                                   f"reference's C# integer path (dotnet absent)"},
+                                   f"reference's C# integer path (dotnet absent)", "host": host_cpu()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
