@@ -241,10 +241,14 @@ shield_status shield_qmatmul_device(shield_ctx *ctx, int32_t device, const char 
  * and larger calls fail with SHIELD_ERR_ARG before touching the GPU.
  * d_x (M x cols f32) and d_y (M x rows f32) are the caller's device buffers.
  * The first call on a GPU looks up the array's device address for that GPU;
- * make that first call before any stream capture.  All calls on a GPU share
- * the one array and it keeps the last call's contents: calls that may
- * overlap on the GPU (other host threads, other contexts) race and must be
- * serialized by the caller.  The call returns after its work completes.
+ * make that first call before any stream capture.  The address is kept for
+ * the life of the process: do not go on using the library on a device after
+ * cudaDeviceReset (or anything else that destroys its primary context).
+ * All calls on a GPU share the one array and it keeps the last call's
+ * contents: calls that may overlap on the GPU (other host threads, other
+ * contexts) race and must be serialized by the caller.  The kernel is chosen
+ * as for the other GEMM entry points (shield_set_gemm_path).  The call returns
+ * after its work completes.
  */
 #define SHIELD_NOALLOC_MAX_ELEMENTS (1 << 21)
 shield_status shield_qmatmul_noalloc(shield_ctx *ctx, int32_t device, const char *weight, const float *d_x,
@@ -299,6 +303,8 @@ typedef struct shield_timing {
     int64_t requests;       /* requests scored */
     int64_t h2d_bytes;      /* host->device bytes of scoring calls */
     int64_t d2h_bytes;      /* device->host bytes of scoring calls */
+    double attn_ms;         /* device time of the attention kernels (level 2 only) */
+    double attn_flops;      /* their algorithmic flops: 4 * heads * head_dim per (query, key) pair */
 } shield_timing;
 
 /* level 0: off; 1: forward intervals and counters; 2: also every GEMM launch. */

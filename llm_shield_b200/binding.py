@@ -49,7 +49,7 @@ class ShieldTiming(C.Structure):
     _fields_ = [("forward_ms", C.c_double), ("gemm_ms", C.c_double), ("gemm_ops", C.c_double),
                 ("gemm_bytes", C.c_double), ("gemm_launches", C.c_int64), ("kernel_launches", C.c_int64),
                 ("tokens", C.c_int64), ("requests", C.c_int64), ("h2d_bytes", C.c_int64),
-                ("d2h_bytes", C.c_int64)]
+                ("d2h_bytes", C.c_int64), ("attn_ms", C.c_double), ("attn_flops", C.c_double)]
 
 
 EXPORTS = [

@@ -186,8 +186,8 @@ struct Scratch {  // grow-on-demand buffers of the single-GEMM entry points
 struct Timing {
     int level = 0;
     std::vector<cudaEvent_t> pool;
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> fwd, gemm;
-    double gemm_ops = 0, gemm_bytes = 0;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> fwd, gemm, attn;
+    double gemm_ops = 0, gemm_bytes = 0, attn_flops = 0;
     int64_t gemm_launches = 0, launches = 0, tokens = 0, requests = 0, h2d = 0, d2h = 0;
     cudaEvent_t event() {
         if (pool.empty()) {
@@ -202,12 +202,14 @@ struct Timing {
     void recycle() {
         for (auto &p : fwd) { pool.push_back(p.first); pool.push_back(p.second); }
         for (auto &p : gemm) { pool.push_back(p.first); pool.push_back(p.second); }
+        for (auto &p : attn) { pool.push_back(p.first); pool.push_back(p.second); }
         fwd.clear();
         gemm.clear();
+        attn.clear();
     }
     void reset() {
         recycle();
-        gemm_ops = gemm_bytes = 0;
+        gemm_ops = gemm_bytes = attn_flops = 0;
         gemm_launches = launches = tokens = requests = h2d = d2h = 0;
     }
     ~Timing() {
@@ -526,6 +528,13 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         if (cur.nw > 0) groups.push_back(cur);
     }
     const int n_work = (int)(work.size() / 2);
+    // algorithmic attention flops of one layer: q.k and p.v, 2 flops per
+    // multiply-add, over every (query, key) pair a causal row attends to
+    double attn_flops_layer = 0;
+    for (int r = 0; r < R; r++) {
+        const double len = B.len[r], pre = pre_of(r);
+        attn_flops_layer += 4.0 * c.n_heads * c.head_dim * (len * pre + len * (len + 1) / 2);
+    }
     if (2 * n_work + 12 * R + 4 > ATT_INTS_PER_TOKEN * b.cap)
         throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
     int32_t *ha = b.h_att;
@@ -677,10 +686,21 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         A.scale = scale;
         if (any_append)
             count_launch(d), check_launch(launch_append_kv(A, d_app, R, M, (int)c.kvdim(), s), "append to KV caches");
+        cudaEvent_t a0 = nullptr, a1 = nullptr;
+        if (T.level >= 2) {
+            a0 = T.event();
+            a1 = T.event();
+            if (a0) cudaEventRecord(a0, s);
+        }
         for (const AttGroup &ag : groups) {
             d.timing.launches += 3;
             A.work = d_work + ag.w0;
             check_launch(launch_attention(A, ag.nw, c.head_dim, s), "attention");
+        }
+        if (a0 && a1) {
+            cudaEventRecord(a1, s);
+            T.attn.emplace_back(a0, a1);
+            T.attn_flops += attn_flops_layer;
         }
         cap(l, SHIELD_ACT_ATTN_WEIGHTED, b.ctx, c.qdim());
         QAct qc = qact(b, M, c.qdim());
@@ -1662,7 +1682,8 @@ shield_status shield_qmatmul_noalloc(shield_ctx *ctx, int32_t device, const char
                                             std::to_string(noalloc_max_elements()) + " activation elements");
         int32_t err = 0;
         cudaError_t e = launch_qmatmul_noalloc(W.w, d_x, M, d_y, C.gemm_path, &err, d.stream);
-        if (e == cudaErrorNotSupported) throw Error(SHIELD_ERR_UNSUPPORTED, "the tensor-core GEMM does not take this shape");
+        if (e == cudaErrorNotSupported)
+            throw Error(SHIELD_ERR_UNSUPPORTED, "the GEMM kernel selected by shield_set_gemm_path does not take this shape");
         check_launch(e, "no-allocation GEMM");
         if (err) throw Error(SHIELD_ERR_TIMEOUT, "a device-side wait gave up (error word " + std::to_string(err) + ")");
     });
@@ -1756,6 +1777,12 @@ shield_status shield_read_timing(shield_ctx *ctx, int32_t device, shield_timing 
             SHIELD_CUDA(cudaEventElapsedTime(&ms, p.first, p.second));
             t.gemm_ms += ms;
         }
+        for (auto &p : T.attn) {
+            float ms = 0;
+            SHIELD_CUDA(cudaEventElapsedTime(&ms, p.first, p.second));
+            t.attn_ms += ms;
+        }
+        t.attn_flops = T.attn_flops;
         t.gemm_ops = T.gemm_ops;
         t.gemm_bytes = T.gemm_bytes;
         t.gemm_launches = T.gemm_launches;

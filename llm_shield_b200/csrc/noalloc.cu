@@ -68,8 +68,18 @@ cudaError_t launch_qmatmul_noalloc(const DevWeight &w, const float *x, int64_t M
     // the error word keeps the previous call's value: clear it first
     if ((e = cudaMemsetAsync(err, 0, sizeof(int32_t), s)) != cudaSuccess) return e;
     if ((e = launch_quantize(x, M, w.cols, w.cols, q, s)) != cudaSuccess) return e;
+    // the kernel choice of every other GEMM entry point (shield_set_gemm_path):
+    // 0 the few-token kernel, then tensor cores, then CUDA cores; 1 CUDA cores;
+    // 2/3 tensor cores only; 4 the few-token kernel only
     bool done = false;
-    if (path != 1 && gemm_tc_supports(w, M)) {
+    if ((path == 0 || path == 4) && gemv_small_supports(w, M)) {
+        e = launch_gemv_small(w, q, y, w.rows, EPI_STORE, s);
+        if (e == cudaSuccess)
+            done = true;
+        else if (e != cudaErrorNotSupported)
+            return e;
+    }
+    if (!done && path != 1 && path != 4 && gemm_tc_supports(w, M)) {
         e = launch_gemm_tc(w, q, y, w.rows, EPI_STORE, err, s);
         if (e == cudaSuccess)
             done = true;
@@ -77,7 +87,7 @@ cudaError_t launch_qmatmul_noalloc(const DevWeight &w, const float *x, int64_t M
             return e;
     }
     if (!done) {
-        if (path == 2) return cudaErrorNotSupported;
+        if (path >= 2) return cudaErrorNotSupported;
         if ((e = launch_gemm_simt(w, nullptr, w.rows, q, y, w.rows, EPI_STORE, s)) != cudaSuccess) return e;
     }
     if ((e = cudaMemcpyAsync(err_out, err, sizeof(int32_t), cudaMemcpyDeviceToHost, s)) != cudaSuccess) return e;

@@ -145,3 +145,24 @@ def test_unsupported_type_and_bad_sizes_are_rejected(ctx):
     with pytest.raises(binding.ShieldError) as e:
         ctx.upload("blk.0.ffn_down.weight", synth.Q4_0, 64, 64, np.zeros(10, np.uint8))
     assert e.value.code == binding.ERR_ARG
+
+
+@pytest.mark.parametrize("qtype", [synth.Q4_0, synth.Q5_0, synth.Q5_1, synth.Q8_0])
+@pytest.mark.parametrize("rows,cols", SWEEP_SHAPES)
+def test_sweep_shapes_at_prefill_sizes_match_oracle(ctx, qtype, rows, cols):
+    """The isolated-GEMM sweep at M = 512 and 4096 (config 2's prefill
+    sizes), bit-identical to the oracle; at M = 512 also on the raw-block
+    tensor-core kernel alone (path 2)."""
+    w = synth.tensor(qtype, rows, cols, seed=78, stream=rows * 11 + cols)
+    upload(ctx, "blk.0.ffn_up.weight", qtype, rows, cols, w)
+    for M in (512, 4096):
+        x = np.random.default_rng(M + rows).standard_normal((M, cols)).astype(np.float32)
+        expect = oracle.qmatmul(qtype, w, rows, cols, x, M, threads=None)
+        np.testing.assert_array_equal(ctx.qmatmul("blk.0.ffn_up.weight", x, M, rows), expect, err_msg=f"M={M}")
+        if M == 512:
+            ctx.set_gemm_path(2)
+            try:
+                np.testing.assert_array_equal(ctx.qmatmul("blk.0.ffn_up.weight", x, M, rows), expect,
+                                              err_msg="raw blocks, M=512")
+            finally:
+                ctx.set_gemm_path(0)

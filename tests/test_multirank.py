@@ -1,6 +1,7 @@
-"""The benchmark's multi-rank host logic on CPU: two gloo ranks split every
-step's requests without overlap, and the job's numbers are the slowest rank's
-times and the summed counts (the NCCL path does the same on GPUs)."""
+"""The benchmark's multi-rank host logic on CPU: two and four gloo ranks split
+every step's requests without overlap and with balanced device cost
+(longest-processing-time first on S * (1 + S / 8192)), and the job's numbers
+are built from every rank's row (the NCCL path does the same on GPUs)."""
 from __future__ import annotations
 
 import os
@@ -25,35 +26,48 @@ def _rank(rank: int, world: int, port: int, out):
     import torch.distributed as dist
     sys.path.insert(0, str(REPO))
     import bench
+    from llm_shield_b200 import synth
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        steps = [bench.step_slice(s, rank, world, 96) for s in range(3)]
-        got = bench.combine_ranks(dist, 10.0 + rank, 20.0 - rank, 1000 * (rank + 1), 96, 7 + rank, "cpu")
-        out.put((rank, [st.tolist() for st in steps], got))
+        lengths = synth.lognormal_lengths(4096, seed=bench.SET_SEED)
+        steps = [bench.rank_requests(5, s, rank, world, 96, lengths) for s in range(3)]
+        rows = bench.gather_ranks(dist, [1000.0 * (rank + 1), 96, 10.0 + rank], world, device="cpu")
+        out.put((rank, [st.tolist() for st in steps], rows.tolist()))
     finally:
         dist.destroy_process_group()
 
 
-def test_two_gloo_ranks_split_requests_and_combine_numbers():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_split_requests_evenly_and_gather_numbers(world):
     torch = pytest.importorskip("torch")
+    sys.path.insert(0, str(REPO))
+    import bench
+    from llm_shield_b200 import synth
     mp = torch.multiprocessing.get_context("spawn")
     q = mp.Queue()
     port = _free_port()
-    procs = [mp.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [mp.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict()
     for _ in procs:
-        r, steps, got = q.get(timeout=120)
-        res[r] = (steps, got)
+        r, steps, rows = q.get(timeout=120)
+        res[r] = (steps, rows)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    lengths = synth.lognormal_lengths(4096, seed=bench.SET_SEED)
     for s in range(3):
-        a, b = set(res[0][0][s]), set(res[1][0][s])
-        assert not a & b and len(a) == len(b) == 96
-    for r in range(2):
-        fwd, e2e, tokens, reqs, launches = res[r][1]
-        assert (fwd, e2e) == (11.0, 20.0)  # max over ranks
-        assert (tokens, reqs, launches) == (3000, 192, 15)  # sums
+        parts = [set(res[r][0][s]) for r in range(world)]
+        union = set().union(*parts)
+        assert sum(len(p) for p in parts) == len(union) == world * 96  # disjoint, the whole window
+        window = set(((np.arange(world * 96) + s * world * 96) % 4096).tolist())
+        assert union == window
+        loads = [sum(bench.cost(lengths[i]) for i in p) for p in parts]
+        assert max(loads) / (sum(loads) / world) < 1.01  # within 1% of an even split
+    for r in range(world):
+        rows = np.array(res[r][1])
+        assert rows.shape == (world, 3)
+        np.testing.assert_array_equal(rows[:, 0], 1000.0 * (np.arange(world) + 1))
+        assert rows[:, 2].max() == 10.0 + world - 1

@@ -5,12 +5,17 @@ Callers that hand all GPU memory to their own pool, or that may not allocate
 on their request path, use it instead of shield_qmatmul_device; its scratch
 is a fixed device array inside the library.  This file is collected last so
 that a run stopping at its first failure has already run every other test.
+
+Each case is checked against the allocating entry point and against the CPU
+oracle (the reference's integer GEMM arithmetic), bit for bit: the kernels
+are the same, only where their scratch lives differs.
 """
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
+import oracle
 from llm_shield_b200 import binding, synth
 from helpers import random_weights
 
@@ -38,25 +43,38 @@ def _run(ctx, torch, name, x, rows, noalloc):
     return dy.cpu().numpy()
 
 
-def test_noalloc_matches_the_allocating_entry_point_on_consecutive_calls(ctx):
-    """Two calls in a row (tensor-core shape, then a CUDA-core shape with a
-    different type) each give exactly what shield_qmatmul_device gives: the
-    shared scratch keeps the previous call's contents, which must not leak."""
+# (type, rows, cols, M, weight name): the tensor-core kernel on the raw blocks
+# (M = 200), on the once-unpacked layer copy (M = 600 at K = 3072, just under
+# the scratch limit), the few-token kernel (M = 5), and the CUDA-core kernel
+# (K = 256 has no tensor-core tile)
+CASES = [(synth.Q4_0, 256, 3072, 200, "blk.0.attn_q.weight"),
+         (synth.Q5_1, 100, 256, 13, "blk.0.attn_k.weight"),
+         (synth.Q4_0, 512, 3072, 600, "blk.0.ffn_gate.weight"),
+         (synth.Q8_0, 384, 3072, 5, "blk.0.ffn_up.weight")]
+
+
+def test_noalloc_matches_the_allocating_entry_point_and_the_oracle(ctx):
+    """Calls in a row, each equal to shield_qmatmul_device and to the oracle:
+    the shared scratch keeps the previous call's contents, which must not
+    leak into the next call."""
     torch = pytest.importorskip("torch")
-    cases = [(synth.Q4_0, 256, 3072, 200, "blk.0.attn_q.weight"),
-             (synth.Q5_1, 100, 256, 13, "blk.0.attn_k.weight")]
-    for i, (qtype, rows, cols, M, name) in enumerate(cases):
+    weights = {}
+    for i, (qtype, rows, cols, M, name) in enumerate(CASES):
+        assert M * cols <= LIMIT
         w = random_weights(qtype, rows, cols, seed=40 + i)
+        weights[name] = w
         ctx.upload(name, qtype, rows, cols, w)
+    for i, (qtype, rows, cols, M, name) in enumerate(CASES):
         x = np.random.default_rng(i).standard_normal((M, cols)).astype(np.float32)
         got = _run(ctx, torch, name, x, rows, noalloc=True)
-        ref = _run(ctx, torch, name, x, rows, noalloc=False)
-        np.testing.assert_array_equal(got, ref)
-    # and the first shape again, after the second call overwrote the scratch
-    qtype, rows, cols, M, name = cases[0]
+        np.testing.assert_array_equal(got, _run(ctx, torch, name, x, rows, noalloc=False), err_msg=name)
+        np.testing.assert_array_equal(got, oracle.qmatmul(qtype, weights[name], rows, cols, x, M), err_msg=name)
+    # the first shape again, after the other calls overwrote the scratch
+    qtype, rows, cols, M, name = CASES[0]
     x = np.random.default_rng(7).standard_normal((M, cols)).astype(np.float32)
-    np.testing.assert_array_equal(_run(ctx, torch, name, x, rows, noalloc=True),
-                                  _run(ctx, torch, name, x, rows, noalloc=False))
+    got = _run(ctx, torch, name, x, rows, noalloc=True)
+    np.testing.assert_array_equal(got, _run(ctx, torch, name, x, rows, noalloc=False))
+    np.testing.assert_array_equal(got, oracle.qmatmul(qtype, weights[name], rows, cols, x, M))
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
@@ -69,3 +87,20 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
     with pytest.raises(binding.ShieldError) as e:
         ctx.qmatmul_noalloc("blk.0.attn_v.weight", dx.data_ptr(), M, dy.data_ptr())
     assert e.value.code == binding.ERR_ARG and "scratch limit" in str(e.value)
+
+
+def test_noalloc_follows_the_selected_kernel(ctx):
+    """shield_set_gemm_path applies here too: the few-token kernel alone
+    (path 4) refuses 17 tokens, as the allocating entry points do."""
+    torch = pytest.importorskip("torch")
+    rows, cols = 128, 3072
+    ctx.upload("blk.0.attn_output.weight", synth.Q4_0, rows, cols, random_weights(synth.Q4_0, rows, cols, seed=9))
+    dx = torch.zeros((17, cols), dtype=torch.float32, device="cuda")
+    dy = torch.zeros((17, rows), dtype=torch.float32, device="cuda")
+    ctx.set_gemm_path(4)
+    try:
+        with pytest.raises(binding.ShieldError) as e:
+            ctx.qmatmul_noalloc("blk.0.attn_output.weight", dx.data_ptr(), 17, dy.data_ptr())
+        assert e.value.code == binding.ERR_UNSUPPORTED
+    finally:
+        ctx.set_gemm_path(0)
