@@ -76,6 +76,8 @@ def parse(argv=None):
     ap.add_argument("--gemm-path", type=int, default=0, help="shield_set_gemm_path for the run")
     ap.add_argument("--decode", default="", help="decode mode: comma list of sequence counts")
     ap.add_argument("--int8-peak", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="model configs: first N layers only (profiling a small case)")
+    ap.add_argument("--requests", type=int, default=0, help="configs 3 and 4: first N requests of the set only")
     return ap.parse_args(argv)
 
 
@@ -199,11 +201,12 @@ def host_cpu() -> dict:
 
 # ------------------------------------------------------------ workloads
 
-def model_spec(config: int):
+def model_spec(config: int, layers: int = 0):
     import dataclasses
     from llm_shield_b200 import synth
     qtype = {1: synth.Q4_0, 3: synth.Q5_1, 4: synth.Q8_0, 5: synth.Q4_0}[config]
-    return dataclasses.replace(synth.SHIELDSTRAL_3B, qtype=qtype)
+    spec = dataclasses.replace(synth.SHIELDSTRAL_3B, qtype=qtype)
+    return dataclasses.replace(spec, n_layers=layers) if layers else spec
 
 
 WORKLOAD = {
@@ -214,8 +217,9 @@ WORKLOAD = {
 }
 
 
-def request_set(config: int, vocab: int):
-    """(ids, offsets, lengths) of the config's seeded request set."""
+def request_set(config: int, vocab: int, limit: int = 0):
+    """(ids, offsets, lengths) of the config's seeded request set (configs 3
+    and 4: its first `limit` requests when limit > 0)."""
     from llm_shield_b200 import synth
     if config == 5:
         lengths = synth.lognormal_lengths(4096, seed=SET_SEED)
@@ -225,6 +229,8 @@ def request_set(config: int, vocab: int):
         lengths = np.full(16, 4096, np.int64)
     else:
         lengths = np.array([256], np.int64)
+    if limit and config in (3, 4):
+        lengths = lengths[:limit]
     rng = np.random.default_rng(SET_SEED + config)
     ids = rng.integers(synth.FIRST_ORDINARY_ID, vocab, size=int(lengths.sum()), dtype=np.int32)
     offsets = np.zeros(lengths.size + 1, np.int64)
@@ -330,6 +336,28 @@ def gather_ranks(dist, values, world: int, device: str = "cuda") -> np.ndarray:
     return torch.stack(out).cpu().numpy()
 
 
+def model_from_gguf(spec, dist, local: int):
+    """The config's model written once per node as a GGUF file (by local rank
+    0, in the temp directory) and mapped back read-only by every rank, so the
+    upload reads each tensor from the file's mapping as GgufFile.GetTensorPointer
+    hands it over (Gguf/GgufFile.cs:195-199). Returns (tensors, file, note)."""
+    import tempfile
+    from llm_shield_b200 import gguf_file, synth
+    path = Path(tempfile.gettempdir()) / f"shield_bench_{spec.qtype}_{spec.n_layers}_{os.getppid()}.gguf"
+    err = None
+    if local == 0:
+        try:
+            gguf_file.write_model(path, spec)
+        except OSError as e:
+            err = str(e)
+    if dist:
+        dist.barrier()
+    if err is None and path.exists():
+        g = gguf_file.GgufFile(path)
+        return g.tensors(), g, f"mapped GGUF file {path.name} ({path.stat().st_size} bytes)"
+    return synth.make_model(spec), None, f"in-memory tensors (writing the GGUF file failed: {err})"
+
+
 def run_model(args) -> int:
     rank, world, local, local_world = dist_env()
     import torch
@@ -339,9 +367,9 @@ def run_model(args) -> int:
 
     cores = len(os.sched_getaffinity(0))
     os.environ.setdefault("SHIELD_SYNTH_THREADS", str(max(1, cores // max(1, local_world))))
-    spec = model_spec(args.config)
-    tensors = synth.make_model(spec)
-    ids, offsets, lengths = request_set(args.config, spec.vocab)
+    spec = model_spec(args.config, args.layers)
+    tensors, gfile, source = model_from_gguf(spec, dist, local)
+    ids, offsets, lengths = request_set(args.config, spec.vocab, args.requests)
 
     ctx = binding.ShieldContext(1 << local)
     ctx.set_config(spec, max_positions=4096, max_batch_tokens=args.max_batch_tokens)
@@ -396,13 +424,20 @@ def run_model(args) -> int:
     tokens_all, reqs_all = int(per_rank[:, 0].sum()), int(per_rank[:, 1].sum())
     line = model_line(args, world, spec, tokens_all, reqs_all, fwd_ms, e2e_max, per_rank, g, peak8)
     line["upload"] = {"seconds": upload_s, "bytes": upload_bytes, "gb_per_s": upload_bytes / upload_s / 1e9,
-                      "what": "every GGUF tensor host->GPU, plus the derived planes built there"}
+                      "what": "every GGUF tensor host->GPU, plus the derived planes built there",
+                      "source": source}
     line["clocks"] = clocks.summary()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_model_sample(args.config, spec, tensors, ids, offsets)
     ctx.close()
     if dist:
+        dist.barrier()
         dist.destroy_process_group()
+    if gfile is not None:
+        path = gfile.path
+        gfile.close()
+        if local == 0:
+            path.unlink(missing_ok=True)
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
@@ -458,7 +493,8 @@ def model_line(args, world, spec, tokens, reqs, fwd_ms, e2e_ms, per_rank, g, pea
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+f32",
         "data": "synthetic (seeded N(0,0.02) weights quantized as gguf-py does; uniform non-special ids)",
         "verdicts_per_s": reqs / (fwd_ms * 1e-3),
-        "config": {"workload": WORKLOAD[args.config], "model": MODEL_DESC,
+        "config": {"workload": WORKLOAD[args.config] + (f", first {args.requests} requests" if args.requests else ""),
+                   "model": MODEL_DESC + (f", first {spec.n_layers} layers only" if args.layers else ""),
                    "weights": synth.TYPE_NAMES[spec.qtype],
                    "per_rank_step": (f"{args.batch} requests of the set, LPT-balanced across ranks"
                                      if args.config == 5 else "the whole set"),

@@ -126,10 +126,11 @@ static void dev_free(T *&p) {
     p = nullptr;
 }
 
-// int32 words of attention metadata per token of capacity: the work list
-// (<= 2 per token + 2 per request) and per request start, len, pre (3), scores
-// base (2), cache keys, values and stride (6) and the append flag (1)
-constexpr int64_t ATT_INTS_PER_TOKEN = 16;
+// int32 words of attention metadata per token of capacity (plus ATT_INTS_EXTRA):
+// per work item (at most one per token and one per request) its request and
+// first query (2) and scratch offset (2); per request start, len, pre (3),
+// cache keys, values and stride (6) and the append flag (1)
+constexpr int64_t ATT_INTS_PER_TOKEN = 16, ATT_INTS_EXTRA = 64;
 
 struct Buffers {
     int64_t cap = 0;  // tokens
@@ -413,13 +414,14 @@ static void ensure_buffers(Ctx &C, Device &d) {
     SHIELD_CUDA(cudaMemsetAsync(d.buf.err, 0, 4, d.stream));
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_meta, (size_t)(4 * T) * 4));
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_logits, (size_t)(T * 64) * 4));
-    // attention scores: at least one longest request, at most ~4 GiB beyond that
-    int64_t one = (int64_t)c.n_heads * c.max_positions * score_row_stride(c.max_positions);
+    // attention scratch: at least one work item of the longest request, at
+    // most 4 GiB (a micro-batch needing more is attended in several launches)
+    int64_t one = attention_scratch_floats(c.max_positions, c.n_kv_heads);
     int64_t all = std::min<int64_t>((int64_t)1 << 30, (int64_t)c.n_heads * T * c.max_positions);
     d.buf.scores_cap = std::max(one, all);
     dev_alloc(d.buf.scores, (size_t)d.buf.scores_cap);
-    dev_alloc(d.buf.att, (size_t)(ATT_INTS_PER_TOKEN * T));
-    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_att, (size_t)(ATT_INTS_PER_TOKEN * T) * 4));
+    dev_alloc(d.buf.att, (size_t)(ATT_INTS_PER_TOKEN * T + ATT_INTS_EXTRA));
+    SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_att, (size_t)(ATT_INTS_PER_TOKEN * T + ATT_INTS_EXTRA) * 4));
     d.buf.cap = T;
 }
 
@@ -500,30 +502,35 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     }
     const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_last = b.meta + 3 * M;
 
-    // attention: requests grouped so each group's S x S scores per head fit the
-    // scratch; one work item per (request, 128/G query tokens)
+    // attention: one work item per (request, 128/G query tokens), longest
+    // first (the CTAs of long rows start early instead of forming a tail), in
+    // groups whose scratch fits the buffer
     const int G = c.n_heads / c.n_kv_heads, QT = attention_rows_per_cta() / G;
     struct AttGroup { int w0, nw; };
+    struct AttItem { int64_t kend; int32_t r, q0; };
+    std::vector<AttItem> items;
+    for (int r = 0; r < R; r++)
+        for (int q0 = 0; q0 < B.len[r]; q0 += QT)
+            items.push_back({(int64_t)pre_of(r) + std::min(q0 + QT, B.len[r]), r, q0});
+    std::stable_sort(items.begin(), items.end(), [](const AttItem &a, const AttItem &b) { return a.kend > b.kend; });
     std::vector<AttGroup> groups;
     std::vector<int32_t> work;
-    std::vector<int64_t> rbase(R);
+    std::vector<int64_t> wbase;
     {
         int64_t used = 0;
         AttGroup cur{0, 0};
-        for (int r = 0; r < R; r++) {
-            int64_t need = (int64_t)c.n_heads * B.len[r] * score_row_stride(pre_of(r) + B.len[r]);
+        for (const AttItem &it : items) {
+            const int64_t need = attention_scratch_floats(it.kend, c.n_kv_heads);
             if (used + need > b.scores_cap && cur.nw > 0) {
                 groups.push_back(cur);
-                cur = AttGroup{(int)(work.size() / 2), 0};
+                cur = AttGroup{(int)wbase.size(), 0};
                 used = 0;
             }
-            rbase[r] = used;
+            wbase.push_back(used);
             used += need;
-            for (int q0 = 0; q0 < B.len[r]; q0 += QT) {
-                work.push_back(r);
-                work.push_back(q0);
-                cur.nw++;
-            }
+            work.push_back(it.r);
+            work.push_back(it.q0);
+            cur.nw++;
         }
         if (cur.nw > 0) groups.push_back(cur);
     }
@@ -535,7 +542,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         const double len = B.len[r], pre = pre_of(r);
         attn_flops_layer += 4.0 * c.n_heads * c.head_dim * (len * pre + len * (len + 1) / 2);
     }
-    if (2 * n_work + 12 * R + 4 > ATT_INTS_PER_TOKEN * b.cap)
+    if (4 * n_work + 12 * R + 8 > ATT_INTS_PER_TOKEN * b.cap + ATT_INTS_EXTRA)
         throw Error(SHIELD_ERR_RANGE, "attention work list exceeds its buffer");
     int32_t *ha = b.h_att;
     memcpy(ha, work.data(), work.size() * 4);
@@ -546,8 +553,9 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         ha_pre[r] = pre_of(r);
     }
     int64_t base_off = (2 * n_work + 3 * R + 1) / 2 * 2;  // int64 arrays on an 8-byte boundary
-    memcpy(ha + base_off, rbase.data(), (size_t)R * 8);
-    const int64_t ck_off = base_off + 2 * R, cv_off = ck_off + 2 * R, cs_off = cv_off + 2 * R, ap_off = cs_off + 2 * R;
+    memcpy(ha + base_off, wbase.data(), (size_t)n_work * 8);
+    const int64_t ck_off = base_off + 2 * n_work, cv_off = ck_off + 2 * R, cs_off = cv_off + 2 * R,
+                  ap_off = cs_off + 2 * R;
     memcpy(ha + ck_off, ck.data(), (size_t)R * 8);
     memcpy(ha + cv_off, cv.data(), (size_t)R * 8);
     memcpy(ha + cs_off, cstride.data(), (size_t)R * 8);
@@ -555,7 +563,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     size_t att_bytes = (size_t)(ap_off * 4 + R);
     const int2 *d_work = reinterpret_cast<const int2 *>(b.att);
     const int32_t *d_rstart = b.att + 2 * n_work, *d_rlen = d_rstart + R, *d_rpre = d_rlen + R;
-    const int64_t *d_rbase = reinterpret_cast<const int64_t *>(b.att + base_off);
+    const int64_t *d_wbase = reinterpret_cast<const int64_t *>(b.att + base_off);
     const float *const *d_ck = reinterpret_cast<const float *const *>(b.att + ck_off);
     const float *const *d_cv = reinterpret_cast<const float *const *>(b.att + cv_off);
     const int64_t *d_cs = reinterpret_cast<const int64_t *>(b.att + cs_off);
@@ -676,7 +684,6 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         A.req_start = d_rstart;
         A.req_len = d_rlen;
         A.req_pre = d_rpre;
-        A.req_base = d_rbase;
         A.cache_k = d_ck;
         A.cache_v = d_cv;
         A.cache_stride = d_cs;
@@ -693,8 +700,9 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             if (a0) cudaEventRecord(a0, s);
         }
         for (const AttGroup &ag : groups) {
-            d.timing.launches += 3;
+            d.timing.launches += 1;
             A.work = d_work + ag.w0;
+            A.work_base = d_wbase + ag.w0;
             check_launch(launch_attention(A, ag.nw, c.head_dim, s), "attention");
         }
         if (a0 && a1) {

@@ -1,6 +1,8 @@
 // Elementwise and attention kernels of the Ministral forward
 // (MinistralModel.cs:282-482): RoPE, causal GQA attention over a ragged batch
 // of requests, SwiGLU.
+#include <algorithm>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -16,7 +18,9 @@ constexpr int PKT = 32;      // keys per PV tile
 constexpr int LDP = PKT + 4; // padded row of a PV weight tile
 }  // namespace att
 
-__device__ __forceinline__ int64_t score_ld(int64_t S) { return score_row_stride(S); }
+// Scratch row stride of a CTA whose rows attend to kend keys: a multiple of 4
+// floats, so every row starts on a 16-byte boundary.
+__device__ __forceinline__ int64_t att_ld(int64_t kend) { return (kend + 3) & ~int64_t(3); }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
@@ -131,27 +135,35 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 }
 
 // Causal grouped-query attention over a ragged batch (AttendGroup,
-// MinistralModel.cs:372-440), in three kernels that keep the oracle's exact
-// operation order, so the context is bit-identical to it:
-//   k_attn_scores   s = (Σ over 8 FMA chains, folded as Vector.Sum) * scale,
-//                   chain j = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4)
-//   k_attn_softmax  max, shield_expf(s - max), 32 lane-strided partial sums
-//                   folded pairwise, division (Kernels.Softmax)
-//   k_attn_pv       ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
-// One CTA owns 128 query rows of one request and one KV head: 128/G tokens x
-// the G query heads sharing that KV head, so each key and value row is read
-// once per CTA for all of them. A request's queries are its tokens in the
-// batch; its keys are the first pre positions of its cache (the system-prompt
-// cache of SystemPromptCache.cs:51-75, or the request's own sequence, as
+// MinistralModel.cs:372-440) in one kernel that keeps the oracle's exact
+// operation order, so the context is bit-identical to it. One CTA owns 128
+// query rows of one request and one KV head: 128/G tokens x the G query heads
+// sharing that KV head, so each key and value row is read once per CTA for all
+// of them. A request's queries are its tokens in the batch; its keys are the
+// first pre positions of its cache (the system-prompt cache of
+// SystemPromptCache.cs:51-75, or the request's own sequence, as
 // MinistralModel.ForwardAsync attends to KvCache, MinistralModel.cs:183-271)
-// followed by its own tokens, so query token t sits at position pre + t. Scores live in a
-// scratch buffer laid out per request as [head][query][key], rows padded to
-// score_row_stride(pre + len) floats.
+// followed by its own tokens, so query token t sits at position pre + t.
+//
+//   phase 1  s = (Σ over 8 FMA chains, folded as Vector.Sum) * scale, chain j
+//            = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4); every
+//            score goes to the CTA's scratch rows and its row maximum is kept
+//   phase 2  per row: e = shield_expf(s - max) in place, summed as 32
+//            lane-strided partials folded pairwise (Kernels.Softmax)
+//   phase 3  ctx[d] = fma(v[p][d], e[p] / sum, ctx[d]) over p in order
+//            (AddScaled4), the division done once per weight as its tile
+//            arrives in shared memory
+//
+// The scratch rows of a CTA (128 x round_up(kend, 4) floats) are written and
+// read back within its lifetime, so short requests' scores never leave L2.
+// Work items arrive longest first (host side), so the long CTAs of a ragged
+// batch start early instead of forming a tail.
 
-// Per-request view shared by the three kernels.
+// Per-work-item view.
 struct AttView {
     int len, pre, q0, qend, kend;  // queries, cached keys, this CTA's query range, keys it needs
-    int64_t start, base, ld;       // first batch row, scores offset, scores row stride
+    int64_t start, ld;             // first batch row, scratch row stride
+    float *sc;                     // this CTA's 128 scratch rows
     const float *ck, *cv;          // this layer's cached keys and values (pre > 0)
 };
 
@@ -163,10 +175,10 @@ __device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
     w.len = A.req_len[r];
     w.pre = A.req_pre ? A.req_pre[r] : 0;
     w.start = A.req_start[r];
-    w.base = A.req_base[r];
-    w.ld = score_ld(w.pre + w.len);
     w.qend = min(w.q0 + QT, w.len);
     w.kend = w.pre + w.qend;
+    w.ld = att_ld(w.kend);
+    w.sc = A.scores + A.work_base[blockIdx.x] + (int64_t)blockIdx.y * att::R * w.ld;
     w.ck = w.cv = nullptr;
     if (w.pre > 0) {
         const int64_t off = (int64_t)A.layer * A.cache_stride[r];
@@ -182,17 +194,18 @@ __device__ __forceinline__ const float *kv_row(const float *own, const float *ca
     return p < w.pre ? cached + (int64_t)p * kvdim : own + (w.start + p - w.pre) * kvdim;
 }
 
-__global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A) {
+// Phase 1: the CTA's 128 x kend scores into its scratch rows, and each row's
+// maximum into rowmax[] (shared). Keys and the CTA's query rows arrive in
+// chain-major order (see chain_pos) by cp.async, key tiles double-buffered.
+// Thread (warp, rl, kl) owns rows warp*16 + rl + 4a and keys kl + 8b of a tile.
+__device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, float *sm, float *rowmax) {
     using namespace att;
-    extern __shared__ float sm[];
-    float *Qs = sm;  // R x LD, chain-major dims; then two KT x LD key tiles
-    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
-    const AttView w = att_view(A, QT);
+    float *Qs = sm;  // R x LD, then two KT x LD key tiles
+    const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
     const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
     const int tid = threadIdx.x;
     const uint32_t kbase = (uint32_t)__cvta_generic_to_shared(sm + R * LD);
-    // keys arrive already in chain-major order, 16 bytes at a time
     auto load = [&](int st, int kt0) {
 #pragma unroll
         for (int it = 0; it < KT * (HD / 4) / THREADS; it++) {
@@ -202,7 +215,6 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
                        ok ? kv_row(A.kc, w.ck, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.kc, ok);
         }
     };
-    // the CTA's query rows, also chain-major already, with the first key tile
     const uint32_t qbase = (uint32_t)__cvta_generic_to_shared(Qs);
 #pragma unroll 4
     for (int it = 0; it < R * (HD / 4) / THREADS; it++) {
@@ -215,7 +227,15 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
     load(0, 0);
     cp_async_commit();
     const int warp = tid >> 5, lane = tid & 31;
-    const int rl = lane >> 3, kl = lane & 7;  // rows warp*16 + rl + 4a, keys kl + 8b
+    const int rl = lane >> 3, kl = lane & 7;
+    int limit[4];  // keys each of the thread's rows attends to
+    float mx[4];
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        const int row = warp * 16 + rl + 4 * a, tok = w.q0 + row / G;
+        limit[a] = tok < w.len ? w.pre + tok + 1 : 0;
+        mx[a] = -INFINITY;
+    }
     for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += KT, st ^= 1) {
         if (kt0 + KT < w.kend) load(st ^ 1, kt0 + KT);
         cp_async_commit();
@@ -229,14 +249,14 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
 #pragma unroll
             for (int o = 0; o < 16; o++) c[o] = 0;
 #pragma unroll
-            for (int st = 0; st < 32; st += 4) {  // two steps of the pair per 16 bytes
+            for (int s = 0; s < 32; s += 4) {  // two steps of the pair per 16 bytes
                 float4 qa[4], kb[4];
 #pragma unroll
                 for (int a = 0; a < 4; a++)
-                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * 32 + st]);
+                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * 32 + s]);
 #pragma unroll
                 for (int b = 0; b < 4; b++)
-                    kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * 32 + st]);
+                    kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * 32 + s]);
 #pragma unroll
                 for (int a = 0; a < 4; a++)
 #pragma unroll
@@ -263,59 +283,93 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_scores(const AttArgs A
         for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(lo_f(c2[o]), hi_f(c2[o])));
 #pragma unroll
         for (int a = 0; a < 4; a++) {
-            const int row = warp * 16 + rl + 4 * a, i = row / G, g = row % G, tok = w.q0 + i;
-            if (tok >= w.len) continue;
-            float *dst = A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld;
+            float *dst = w.sc + (int64_t)(warp * 16 + rl + 4 * a) * w.ld;
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const int p = kt0 + kl + 8 * b;
-                if (p <= w.pre + tok) dst[p] = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), A.scale);
+                if (p < limit[a]) {
+                    const float s = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), A.scale);
+                    dst[p] = s;
+                    mx[a] = fmaxf(mx[a], s);
+                }
             }
         }
         __syncthreads();
     }
+    // the 8 lanes sharing a row (kl) hold its maxima over disjoint keys
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        float m = mx[a];
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        if (kl == 0) rowmax[warp * 16 + rl + 4 * a] = m;
+    }
 }
 
-// One warp per row at a time: rows of the CTA's 128-row tile, in turn.
-__global__ void __launch_bounds__(att::THREADS) k_attn_softmax(const AttArgs A) {
+// Phase 2: one warp per row, rows warp, warp + 8, ..: e = exp(s - max) in
+// place summed as 32 lane-strided partials, then w = e / sum in place; a row
+// whose maximum is not finite becomes uniform (Kernels.Softmax).
+__device__ __forceinline__ void attn_softmax(const AttArgs &A, const AttView &w, const float *rowmax) {
     using namespace att;
-    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
-    const AttView w = att_view(A, QT);
-    const int h = blockIdx.y;
+    const int G = A.n_heads / A.n_kv_heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int row = warp; row < R; row += THREADS / 32) {
-        const int i = row / G, g = row % G, tok = w.q0 + i;
+        const int tok = w.q0 + row / G;
         if (tok >= w.len) continue;
         const int limit = w.pre + tok + 1;
-        float *s = A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld;
-        float mx = -INFINITY;
-        for (int p = lane; p < limit; p += 32) mx = fmaxf(mx, s[p]);
-        mx = warp_max(mx);
+        const float mx = rowmax[row];
+        float *s = w.sc + (int64_t)row * w.ld;
+        // phase 3 loads weights in 4-key granules: the keys after the row's own
+        // position in its last granule must read as 0
+        if (lane < ((limit + 3) & ~3) - limit) s[limit + lane] = 0.0f;
+        if (!isfinite(mx)) {
+            const float u = __fdiv_rn(1.0f, (float)limit);
+            for (int p = lane; p < limit; p += 32) s[p] = u;
+            continue;
+        }
+        // lane j sums keys j, j + 32, .. in order; eight of its keys are
+        // loaded together so the pass is not one round trip per key
         float sum = 0.0f;
-        for (int p = lane; p < limit; p += 32) {
-            float e = shield_expf(__fsub_rn(s[p], mx));
+        int p = lane;
+        for (; p + 7 * 32 < limit; p += 8 * 32) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = s[p + 32 * u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float e = shield_expf(__fsub_rn(v[u], mx));
+                s[p + 32 * u] = e;
+                sum = __fadd_rn(sum, e);
+            }
+        }
+        for (; p < limit; p += 32) {
+            const float e = shield_expf(__fsub_rn(s[p], mx));
             s[p] = e;
             sum = __fadd_rn(sum, e);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-        __syncwarp();
-        for (int p = lane; p < limit; p += 32) s[p] = __fdiv_rn(s[p], sum);
-        for (int p = limit + lane; p < w.kend; p += 32) s[p] = 0.0f;  // keys the PV tile walks past
-        __syncwarp();
+        for (p = lane; p + 7 * 32 < limit; p += 8 * 32) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = s[p + 32 * u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) s[p + 32 * u] = __fdiv_rn(v[u], sum);
+        }
+        for (; p < limit; p += 32) s[p] = __fdiv_rn(s[p], sum);
     }
 }
 
-// ctx[row][d] = sum over keys p in order of fma(v[p][d], w[row][p], .)
-// (MinistralModel.cs:372-440). Key tiles of V and of the softmax weights are
-// double-buffered in shared memory by cp.async; thread (tr, td) owns rows
-// tr + 32a and dims td*4 + 32e (a, e < 4).
-__global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
+// Phase 3: ctx[row][d] = sum over keys p in order of fma(v[p][d], w[row][p], .)
+// with w = e / sum (MinistralModel.cs:372-440). Key tiles of V and of the
+// exp values are double-buffered in shared memory by cp.async; each weight
+// tile is divided once in place (masked keys to 0) before use. Thread (tr, td)
+// owns rows tr + 32a and dims td*4 + 32e (a, e < 4).
+__device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, float *sm) {
     using namespace att;
-    extern __shared__ float sm[];
     constexpr int V_FLOATS = PKT * LD, W_FLOATS = R * LDP;
-    const int G = A.n_heads / A.n_kv_heads, QT = R / G;
-    const AttView w = att_view(A, QT);
+    const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
     const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
     const int tid = threadIdx.x, tr = tid >> 3, td = tid & 7;
@@ -333,10 +387,9 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
 #pragma unroll
         for (int it = 0; it < R * (PKT / 4) / THREADS; it++) {
             const int idx = tid + it * THREADS, row = idx / (PKT / 4), c4 = idx % (PKT / 4);
-            const int i = row / G, g = row % G, tok = w.q0 + i, p = kt0 + c4 * 4;
-            const bool ok = tok < w.len && p < w.kend;
-            cp_async16(wb + (uint32_t)(row * LDP + c4 * 4) * 4,
-                       ok ? A.scores + w.base + ((int64_t)(h * G + g) * w.len + tok) * w.ld + p : A.scores, ok);
+            const int tok = w.q0 + row / G, p = kt0 + c4 * 4;
+            const bool ok = tok < w.len && p <= w.pre + tok;
+            cp_async16(wb + (uint32_t)(row * LDP + c4 * 4) * 4, ok ? w.sc + (int64_t)row * w.ld + p : w.sc, ok);
         }
     };
     // c2[a][2e + h]: dims td*4 + 32e + 2h + {0, 1} of row tr + 32a, as f32 pairs;
@@ -368,8 +421,8 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
-        const uint32_t vs = sbase + (uint32_t)(st * (V_FLOATS + W_FLOATS)) * 4;
         const float *W = Ws(st);
+        const uint32_t vs = sbase + (uint32_t)(st * (V_FLOATS + W_FLOATS)) * 4;
         const int kn = min(PKT, w.kend - kt0);
         int kk = 0;
         for (; kk + 4 <= kn; kk += 4) {
@@ -401,21 +454,25 @@ __global__ void __launch_bounds__(att::THREADS, 2) k_attn_pv(const AttArgs A) {
     }
 }
 
+__global__ void __launch_bounds__(att::THREADS, 2) k_attn(const AttArgs A) {
+    extern __shared__ float sm[];
+    __shared__ float rowmax[att::R];
+    const AttView w = att_view(A, att::R / (A.n_heads / A.n_kv_heads));
+    attn_scores(A, w, sm, rowmax);
+    __syncthreads();
+    attn_softmax(A, w, rowmax);
+    __syncthreads();
+    attn_pv(A, w, sm);
+}
+
 cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, cudaStream_t s) {
     using namespace att;
     if (n_work == 0) return cudaSuccess;
     if (head_dim != HD || A.n_heads % A.n_kv_heads || R % (A.n_heads / A.n_kv_heads)) return cudaErrorInvalidValue;
-    const size_t smem_s = (size_t)(R + 2 * KT) * LD * 4, smem_pv = (size_t)2 * (PKT * LD + R * LDP) * 4;
-    cudaError_t e = cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
+    const size_t smem = std::max((size_t)(R + 2 * KT) * LD * 4, (size_t)2 * (PKT * LD + R * LDP) * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)n_work, (unsigned)A.n_kv_heads);
-    k_attn_scores<<<grid, THREADS, smem_s, s>>>(A);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_attn_softmax<<<grid, THREADS, 0, s>>>(A);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pv);
-    if (e != cudaSuccess) return e;
-    k_attn_pv<<<grid, THREADS, smem_pv, s>>>(A);
+    k_attn<<<dim3((unsigned)n_work, (unsigned)A.n_kv_heads), THREADS, smem, s>>>(A);
     return cudaGetLastError();
 }
 

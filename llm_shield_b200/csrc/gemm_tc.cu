@@ -33,6 +33,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -118,6 +120,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             if (clock64() - t0 > 4000000000LL) {
                 *abort_flag = 1;
                 if (err) atomicExch(err, 3);
+                return false;
+            }
+        }
+    }
+}
+
+// The same kind of bounded wait for a whole warp: every lane polls and a
+// vote makes the outcome warp-uniform, so a loop around it needs no
+// reconvergence point. It gives up after 2^26 polls (a quarter of a second
+// or more; a preempted CTA does not poll, so time it is not running does not
+// count), raising the abort flag and the error word.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort_flag, int32_t *err) {
+    for (uint32_t i = 0;; i++) {
+        if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
+        if ((i & 255) == 255) {
+            int stop = *abort_flag ? 1 : (i >= (1u << 26) ? 2 : 0);
+            stop = __shfl_sync(0xffffffffu, stop, 0);
+            if (stop) {
+                if (stop == 2 && (threadIdx.x & 31) == 0) {
+                    *abort_flag = 1;
+                    if (err) atomicExch(err, 3);
+                }
                 return false;
             }
         }
@@ -292,9 +316,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             // filled by TMA (PRE), or by the unpackers plus the producer's
             // TMA of the activation scales
             mbar_init(sc_full(s), PRE ? 1 : UNPACK_THREADS + (DOTS ? 0 : 1));
-            mbar_init(sc_empty(s), EPI_WARPS);
+            mbar_init(sc_empty(s), EPI_WARPS * 32);
         }
-        for (int s = 0; s < NSLOT; s++) mbar_init(t_empty(s), EPI_WARPS);
+        for (int s = 0; s < NSLOT; s++) mbar_init(t_empty(s), EPI_WARPS * 32);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -473,98 +497,114 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         uint32_t cc = 0;               // chunks consumed, over all tiles
         uint32_t dstage = 0, dphase = 0;  // next block pair's commit barrier and parity
         bool ok = true;
+        constexpr bool PAIRS = has_offset(TYPE);
         for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
             const bool warp_live = m0 + q * 32 < M;
-            float f[32];  // [token k][column 2i + e]
+            // the accumulators of columns tcol + 8i and tcol + 8i + 1 of token k:
+            // f[8k + 2i + e] as scalars, or (offset types, whose two chain steps
+            // per block pair up better) f2[4k + i] as one f32 pair, each lane of
+            // a packed fma being the scalar fma of its output
+            float f[PAIRS ? 1 : 32];
+            uint64_t f2[PAIRS ? 16 : 1];
 #pragma unroll
-            for (int i = 0; i < 32; i++) f[i] = 0.0f;
-            for (int c = 0; c < nchunks; c++, cc++) {
+            for (int i = 0; i < (PAIRS ? 1 : 32); i++) f[i] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < (PAIRS ? 16 : 1); i++) f2[i] = 0;
+            // One chunk of CHUNK blocks. LIVE: the warp's tokens exist (a warp
+            // past the last token only keeps the barriers in step). The block
+            // loop has no divergent branch: its waits are warp-uniform votes
+            // and every lane arrives on the release barriers.
+            auto chunk = [&](auto live, int c) -> bool {
+                constexpr bool LIVE = decltype(live)::value;
                 const int ss = cc % SC_STAGES;
-                if (!__all_sync(0xffffffffu, mbar_wait(sc_full(ss), (cc / SC_STAGES) & 1, abort_flag, err))) {
-                    ok = false;
-                    break;
-                }
+                if (!mbar_wait_warp(sc_full(ss), (cc / SC_STAGES) & 1, abort_flag, err)) return false;
                 const uint32_t sc_s = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
                 const uint32_t w_s = sc_s + w_off, dlo_s = sc_s + d_lo, dhi_s = sc_s + d_hi;
 #pragma unroll
                 for (int j = 0; j < CHUNK; j++) {
                     const int kb = c * CHUNK + j, slot = j % NSLOT;  // chunks start on slot 0
                     if (j % 2 == 0) {
-                        const bool got = mbar_wait(done(dstage), dphase, abort_flag, err);
+                        const bool got = mbar_wait_warp(done(dstage), dphase, abort_flag, err);
                         if (++dstage == STAGES) dstage = 0, dphase ^= 1;
-                        if (!__all_sync(0xffffffffu, got)) {
-                            ok = false;
-                            break;
-                        }
+                        if (!got) return false;
                         tc_fence_after();
                     }
-                    uint64_t w2[4], o2[4];
-                    float dav[4], dsv[4];
-                    if (!DOTS && warp_live) {
+                    if (LIVE) {
+                        uint64_t w2[4], o2[4];
+                        float dav[4], dsv[4];
+                        if (!DOTS) {
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            w2[i] = lds_b64(w_s + j * BN * 4 + 32 * i);
-                            if (has_offset(TYPE)) o2[i] = lds_b64(w_s + (CHUNK + j) * BN * 4 + 32 * i);
-                        }
-                        const uint32_t d_s = (j < 4 ? dlo_s : dhi_s) + 4 * j;
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            dav[k] = lds_f32(d_s + k * 8 * CHUNK * 4);
-                            if (has_offset(TYPE)) dsv[k] = lds_f32(d_s + CHUNK * BM * 4 + k * 8 * CHUNK * 4);
-                        }
-                    }
-#pragma unroll
-                    for (int hh = 0; hh < 2; hh++) {
-                        uint32_t r[16];
-                        tmem_ld16x256(t_lane + ((uint32_t)(16 * hh) << 16) + slot * BN, r);
-                        if (DOTS) {
-#pragma unroll
-                            for (int kk = 0; kk < 2; kk++) {
-                                const int m = m0 + q * 32 + tr + 8 * (2 * hh + kk);
-                                if (m >= M) continue;
-#pragma unroll
-                                for (int i = 0; i < 4; i++)
-#pragma unroll
-                                    for (int e = 0; e < 2; e++) {
-                                        const int n = n0 + tcol + 8 * i + e;
-                                        if (n < N)
-                                            dots[((int64_t)m * N + n) * nb + kb] =
-                                                (int32_t)__uint_as_float(r[4 * i + 2 * kk + e]);
-                                    }
+                            for (int i = 0; i < 4; i++) {
+                                w2[i] = lds_b64(w_s + j * BN * 4 + 32 * i);
+                                if (PAIRS) o2[i] = lds_b64(w_s + (CHUNK + j) * BN * 4 + 32 * i);
                             }
-                        } else if (warp_live) {
+                            const uint32_t d_s = (j < 4 ? dlo_s : dhi_s) + 4 * j;
 #pragma unroll
-                            for (int kk = 0; kk < 2; kk++) {
-                                const int k = 2 * hh + kk;
-                                const uint64_t da2 = pack2u(__float_as_uint(dav[k]), __float_as_uint(dav[k]));
+                            for (int k = 0; k < 4; k++) {
+                                dav[k] = lds_f32(d_s + k * 8 * CHUNK * 4);
+                                if (PAIRS) dsv[k] = lds_f32(d_s + CHUNK * BM * 4 + k * 8 * CHUNK * 4);
+                            }
+                        }
 #pragma unroll
-                                for (int i = 0; i < 4; i++) {
-                                    // the two scale products as one f32x2 multiply, the
-                                    // accumulations as scalar fma on the loaded words
-                                    const uint64_t p2 = mul2(w2[i], da2);
-                                    float *fk = f + 8 * k + 2 * i;
-                                    fk[0] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk]), lo_f(p2), fk[0]);
-                                    fk[1] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk + 1]), hi_f(p2), fk[1]);
+                        for (int hh = 0; hh < 2; hh++) {
+                            uint32_t r[16];
+                            tmem_ld16x256(t_lane + ((uint32_t)(16 * hh) << 16) + slot * BN, r);
+                            if (DOTS) {
+#pragma unroll
+                                for (int kk = 0; kk < 2; kk++) {
+                                    const int m = m0 + q * 32 + tr + 8 * (2 * hh + kk);
+                                    if (m >= M) continue;
+#pragma unroll
+                                    for (int i = 0; i < 4; i++)
+#pragma unroll
+                                        for (int e = 0; e < 2; e++) {
+                                            const int n = n0 + tcol + 8 * i + e;
+                                            if (n < N)
+                                                dots[((int64_t)m * N + n) * nb + kb] =
+                                                    (int32_t)__uint_as_float(r[4 * i + 2 * kk + e]);
+                                        }
                                 }
-                                if (has_offset(TYPE)) {
+                            } else {
+#pragma unroll
+                                for (int kk = 0; kk < 2; kk++) {
+                                    const int k = 2 * hh + kk;
+                                    const uint64_t da2 = pack2u(__float_as_uint(dav[k]), __float_as_uint(dav[k]));
 #pragma unroll
                                     for (int i = 0; i < 4; i++) {
-                                        float *fk = f + 8 * k + 2 * i;
-                                        fk[0] = __fmaf_rn(lo_f(o2[i]), dsv[k], fk[0]);
-                                        fk[1] = __fmaf_rn(hi_f(o2[i]), dsv[k], fk[1]);
+                                        // the two scale products as one f32x2 multiply
+                                        const uint64_t p2 = mul2(w2[i], da2);
+                                        if (PAIRS) {
+                                            f2[4 * k + i] = fma2(pack2u(r[4 * i + 2 * kk], r[4 * i + 2 * kk + 1]),
+                                                                 p2, f2[4 * k + i]);
+                                        } else {
+                                            float *fk = f + 8 * k + 2 * i;
+                                            fk[0] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk]), lo_f(p2), fk[0]);
+                                            fk[1] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk + 1]), hi_f(p2),
+                                                              fk[1]);
+                                        }
+                                    }
+                                    if (PAIRS) {
+                                        const uint64_t ds2 = pack2u(__float_as_uint(dsv[k]), __float_as_uint(dsv[k]));
+#pragma unroll
+                                        for (int i = 0; i < 4; i++) f2[4 * k + i] = fma2(o2[i], ds2, f2[4 * k + i]);
                                     }
                                 }
                             }
                         }
                     }
                     tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(t_empty(slot));
+                    mbar_arrive(t_empty(slot));
                 }
-                if (!ok) break;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(sc_empty(ss));
+                mbar_arrive(sc_empty(ss));
+                return true;
+            };
+            for (int c = 0; c < nchunks; c++, cc++) {
+                const bool good = warp_live ? chunk(std::true_type{}, c) : chunk(std::false_type{}, c);
+                if (!good) {
+                    ok = false;
+                    break;
+                }
             }
             if (!ok) break;
             if (!DOTS && !*abort_flag) {
@@ -576,7 +616,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         if (n0 + tcol + 8 * i >= N) break;
-                        float2 v = make_float2(f[8 * k + 2 * i], f[8 * k + 2 * i + 1]);
+                        float2 v = PAIRS ? make_float2(lo_f(f2[4 * k + i]), hi_f(f2[4 * k + i]))
+                                         : make_float2(f[8 * k + 2 * i], f[8 * k + 2 * i + 1]);
                         if (EPI == EPI_ADD) {
                             const float2 o = *reinterpret_cast<const float2 *>(dst + 8 * i);
                             v.x = __fadd_rn(o.x, v.x);

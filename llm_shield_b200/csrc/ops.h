@@ -89,19 +89,22 @@ int64_t noalloc_max_elements();
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
                         cudaStream_t s, bool natural = true);
-// Causal GQA attention of a group of requests (three kernels, see forward_ops.cu).
-// work[i] = {request, first query token}; one CTA per (work item, KV head)
-// covers attention_rows_per_cta() query rows (tokens x the heads of a group).
+// Causal GQA attention of a group of work items (one fused kernel, see
+// forward_ops.cu). work[i] = {request, first query token}; one CTA per (work
+// item, KV head) covers attention_rows_per_cta() query rows (tokens x the
+// heads of a group). Its scores live in the scratch while it runs:
+// attention_scratch_floats(kend) floats per work item from work_base[i],
+// kend = pre + the last query token + 1, the KV heads' rows one after another.
 struct AttArgs {
     const float *qc = nullptr;      // queries after RoPE, chain-major (launch_rope's perm output)
     const float *kc = nullptr;      // keys after RoPE, chain-major
     const float *v = nullptr;
     float *ctx = nullptr;
-    float *scores = nullptr;        // n_heads * Σ len * score_row_stride(pre + len) floats
+    float *scores = nullptr;        // the scratch
     const int2 *work = nullptr;
+    const int64_t *work_base = nullptr;  // scratch offset (floats, a multiple of 4) per work item
     const int32_t *req_start = nullptr, *req_len = nullptr;
     const int32_t *req_pre = nullptr;   // cached positions in front of each request (nullptr: none)
-    const int64_t *req_base = nullptr;  // scores offset per request
     // per request with pre > 0: its cache (the system-prompt prefix or its own
     // sequence), layer 0 row 0 of the keys (chain-major) and values, and the
     // floats from one layer's rows to the next
@@ -124,8 +127,9 @@ cudaError_t launch_append_kv(const AttArgs &args, const uint8_t *append, int n_r
 cudaError_t launch_prefix_state(float *dev_k, float *dev_v, float *snap_k, float *snap_v, int64_t P, int kv_heads,
                                 int head_dim, bool to_device, cudaStream_t s);
 int attention_rows_per_cta();
-// Scores of one (head, query) row are stored with a row stride rounded up to
-// 4 floats, so that every row starts on a 16-byte boundary.
-constexpr int64_t score_row_stride(int64_t S) { return (S + 3) & ~int64_t(3); }
+// Scratch floats of one work item whose rows attend to kend keys, all KV heads.
+inline int64_t attention_scratch_floats(int64_t kend, int n_kv_heads) {
+    return (int64_t)n_kv_heads * attention_rows_per_cta() * ((kend + 3) & ~int64_t(3));
+}
 
 }  // namespace shield

@@ -12,20 +12,28 @@ incremental forwards equal to whole ones, Score consistent with the logits
 """
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import pytest
 
 import oracle
-from llm_shield_b200 import binding, synth
+from llm_shield_b200 import binding, gguf_file, synth
 from helpers import oracle_model
 
 pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")
-def big(shield_lib):
-    spec = synth.SHIELDSTRAL_3B
-    tensors = synth.make_model(spec)
+def big(shield_lib, tmp_path_factory):
+    """The model written as a GGUF file and uploaded from its read-only
+    mapping (GgufFile.GetTensorPointer, GgufFile.cs:195-199); the config comes
+    from the file's metadata (ModelConfig.FromGguf)."""
+    path = gguf_file.write_model(tmp_path_factory.mktemp("gguf") / "shieldstral_q4_0.gguf", synth.SHIELDSTRAL_3B)
+    g = gguf_file.GgufFile(path)
+    spec = dataclasses.replace(synth.SHIELDSTRAL_3B, **{f: getattr(g.spec(), f) for f in (
+        "n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "yes_ids", "no_ids", "qtype")})
+    tensors = g.tensors()
     ctx = binding.ShieldContext(1)
     ctx.set_config(spec, max_positions=4096, max_batch_tokens=16384)
     ctx.upload_model(tensors)
