@@ -38,6 +38,7 @@ class OrcConfig(C.Structure):
         ("vocab", C.c_int32), ("rms_eps", C.c_float), ("rope_half", C.c_int32),
         ("rope_freqs", C.c_float * 256), ("rope_mscale", C.c_float),
         ("attn_temperature_beta", C.c_float), ("rope_orig_ctx", C.c_int32),
+        ("attn_operand_bits", C.c_int32),
     ]
 
 
@@ -215,6 +216,7 @@ class Model:
         c.rope_mscale = cfg["rope_mscale"]
         c.attn_temperature_beta = cfg.get("attn_temperature_beta", 0.0)
         c.rope_orig_ctx = cfg.get("rope_orig_ctx", 0)
+        c.attn_operand_bits = cfg.get("attn_operand_bits", 0)
         self.cfg = cfg
         self._keep = []
         self.h = lib().orc_model_create(C.byref(c))

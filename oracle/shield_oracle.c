@@ -809,6 +809,18 @@ typedef struct {
     float scale;
 } orc_attn_job;
 
+/* x rounded to nearest-even with `bits` explicit mantissa bits (finite x). */
+static inline float orc_round_mantissa(float x, int bits) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    const int drop = 23 - bits;
+    const uint32_t lsb = (u >> drop) & 1u;
+    u += (1u << (drop - 1)) - 1u + lsb;
+    u &= ~((1u << drop) - 1u);
+    memcpy(&x, &u, 4);
+    return x;
+}
+
 /* AttendGroup (MinistralModel.cs:372-440) for one (kv head, query token):
  * every query head sharing the KV head, on an empty cache (startPos = 0). */
 static void orc_attend(void *vctx, int64_t item) {
@@ -818,12 +830,22 @@ static void orc_attend(void *vctx, int64_t item) {
     int qdim = c->n_heads * hd, kvdim = c->n_kv_heads * hd;
     int kvh = (int)(item / J->seq), t = (int)(item % J->seq);
     int limit = t + 1;
+    const int rb = c->attn_operand_bits;
     float *s = (float *)malloc((size_t)limit * 4);
+    float qr[512], kr[512], vr[512];
     for (int g = 0; g < group; g++) {
         int head = kvh * group + g;
         const float *qh = J->q + (int64_t)t * qdim + (int64_t)head * hd;
+        if (rb > 0 && hd <= 512) {
+            for (int d = 0; d < hd; d++) qr[d] = orc_round_mantissa(qh[d], rb);
+            qh = qr;
+        }
         for (int p = 0; p < limit; p++) {
             const float *kp = J->keys + (int64_t)p * kvdim + (int64_t)kvh * hd;
+            if (rb > 0 && hd <= 512) {
+                for (int d = 0; d < hd; d++) kr[d] = orc_round_mantissa(kp[d], rb);
+                kp = kr;
+            }
             /* Kernels.Dot4: 8 lanes of fused multiply-adds, then Vector.Sum */
             float acc[8] = {0};
             int i = 0;
@@ -841,8 +863,12 @@ static void orc_attend(void *vctx, int64_t item) {
          * fma(v, 0, c) == c for finite v except that it may turn a -0 context
          * into +0, so the skip changes no value beyond the sign of a zero. */
         for (int p = 0; p < limit; p++) {
-            float w = s[p];
+            float w = rb > 0 ? orc_round_mantissa(s[p], rb) : s[p];
             const float *vp = J->values + (int64_t)p * kvdim + (int64_t)kvh * hd;
+            if (rb > 0 && hd <= 512) {
+                for (int d = 0; d < hd; d++) vr[d] = orc_round_mantissa(vp[d], rb);
+                vp = vr;
+            }
             for (int d = 0; d < hd; d++) ch[d] = fmaf(vp[d], w, ch[d]); /* Kernels.AddScaled4 */
         }
     }
