@@ -336,26 +336,34 @@ def gather_ranks(dist, values, world: int, device: str = "cuda") -> np.ndarray:
     return torch.stack(out).cpu().numpy()
 
 
-def model_from_gguf(spec, dist, local: int):
+def model_from_gguf(spec, dist, local: int, wait_s: float = 900.0):
     """The config's model written once per node as a GGUF file (by local rank
-    0, in the temp directory) and mapped back read-only by every rank, so the
-    upload reads each tensor from the file's mapping as GgufFile.GetTensorPointer
-    hands it over (Gguf/GgufFile.cs:195-199). Returns (tensors, file, note)."""
+    0, with every host core, in the temp directory; published by an atomic
+    rename) and mapped back read-only by every rank, so the upload reads each
+    tensor from the file's mapping as GgufFile.GetTensorPointer hands it over
+    (Gguf/GgufFile.cs:195-199). The other ranks poll for the file (at most
+    wait_s seconds) rather than wait in a collective with a short timeout.
+    Returns (tensors, file, note)."""
     import tempfile
     from llm_shield_b200 import gguf_file, synth
     path = Path(tempfile.gettempdir()) / f"shield_bench_{spec.qtype}_{spec.n_layers}_{os.getppid()}.gguf"
     err = None
     if local == 0:
+        part = path.with_suffix(".part")
         try:
-            gguf_file.write_model(path, spec)
+            gguf_file.write_model(part, spec)
+            os.replace(part, path)
         except OSError as e:
             err = str(e)
-    if dist:
-        dist.barrier()
+            part.unlink(missing_ok=True)
+    else:
+        t0 = time.monotonic()
+        while not path.exists() and time.monotonic() - t0 < wait_s:
+            time.sleep(0.5)
     if err is None and path.exists():
         g = gguf_file.GgufFile(path)
         return g.tensors(), g, f"mapped GGUF file {path.name} ({path.stat().st_size} bytes)"
-    return synth.make_model(spec), None, f"in-memory tensors (writing the GGUF file failed: {err})"
+    return synth.make_model(spec), None, f"in-memory tensors (the GGUF file is missing: {err or 'not written in time'})"
 
 
 def run_model(args) -> int:
@@ -365,8 +373,8 @@ def run_model(args) -> int:
     dist = init_dist(world)
     from llm_shield_b200 import binding, synth
 
-    cores = len(os.sched_getaffinity(0))
-    os.environ.setdefault("SHIELD_SYNTH_THREADS", str(max(1, cores // max(1, local_world))))
+    # local rank 0 alone synthesizes the model (the others map its file)
+    os.environ.setdefault("SHIELD_SYNTH_THREADS", str(len(os.sched_getaffinity(0))))
     spec = model_spec(args.config, args.layers)
     tensors, gfile, source = model_from_gguf(spec, dist, local)
     ids, offsets, lengths = request_set(args.config, spec.vocab, args.requests)
@@ -431,7 +439,7 @@ def run_model(args) -> int:
         line["cpu_baseline"] = cpu_model_sample(args.config, spec, tensors, ids, offsets)
     ctx.close()
     if dist:
-        dist.barrier()
+        dist.barrier()  # every rank has uploaded before the file goes
         dist.destroy_process_group()
     if gfile is not None:
         path = gfile.path

@@ -71,3 +71,43 @@ def test_gloo_ranks_split_requests_evenly_and_gather_numbers(world):
         assert rows.shape == (world, 3)
         np.testing.assert_array_equal(rows[:, 0], 1000.0 * (np.arange(world) + 1))
         assert rows[:, 2].max() == 10.0 + world - 1
+
+
+def _gguf_rank(local: int, out):
+    sys.path.insert(0, str(REPO))
+    import bench
+    from llm_shield_b200 import synth
+    spec = synth.small_spec(qtype=synth.Q4_0, n_layers=2, seed=17)
+    tensors, gfile, note = bench.model_from_gguf(spec, None, local, wait_s=120)
+    digest = {k: (t["type"], t["rows"], t["cols"], int(np.asarray(t["data"], np.uint64).sum())) for k, t in tensors.items()}
+    out.put((local, gfile is not None, note, digest))
+
+
+def test_model_file_written_once_and_mapped_by_every_rank():
+    """bench.py's per-node hand-off: local rank 0 writes the GGUF file
+    (published by a rename), a rank that starts earlier waits for it, and
+    both upload from a mapping of the same bytes."""
+    torch = pytest.importorskip("torch")
+    from llm_shield_b200 import synth
+    mp = torch.multiprocessing.get_context("spawn")
+    q = mp.Queue()
+    procs = [mp.Process(target=_gguf_rank, args=(r, q)) for r in (1, 0)]  # the reader first
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, mapped, note, digest = q.get(timeout=300)
+        res[r] = (mapped, note, digest)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    spec = synth.small_spec(qtype=synth.Q4_0, n_layers=2, seed=17)
+    want = {k: (t["type"], t["rows"], t["cols"], int(np.asarray(t["data"], np.uint64).sum()))
+            for k, t in synth.make_model(spec).items()}
+    for r in (0, 1):
+        assert res[r][0], res[r][1]
+        assert res[r][2] == want
+    import os
+    import tempfile
+    leftover = Path(tempfile.gettempdir()) / f"shield_bench_{spec.qtype}_{spec.n_layers}_{os.getpid()}.gguf"
+    leftover.unlink(missing_ok=True)
