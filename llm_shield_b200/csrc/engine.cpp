@@ -376,6 +376,52 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
     }
 }
 
+// The Q/K/V projections of a layer (same activations): one tensor-core launch
+// covering all three when the kernel takes them (several tiles of each run
+// side by side, which matters when few tokens make few tiles), else one
+// gemm() each. The outputs are identical either way.
+static void gemm_qkv(Ctx &C, Device &d, const Tensor &wq, const Tensor &wk, const Tensor &wv, const QAct &q,
+                     float *yq, float *yk, float *yv, int64_t ldq, int64_t ldkv) {
+    const DevWeight *ws[3] = {&wq.w, &wk.w, &wv.w};
+    float *ys[3] = {yq, yk, yv};
+    const int64_t lds[3] = {ldq, ldkv, ldkv};
+    const bool tc_path = C.gemm_path == 0 || C.gemm_path == 2 || C.gemm_path == 3;
+    bool grouped = tc_path && !(C.gemm_path == 0 && gemv_small_supports(wq.w, q.M));
+    for (int g = 0; g < 3 && grouped; g++) grouped = gemm_tc_supports(*ws[g], q.M);
+    if (grouped) {
+        Timing &T = d.timing;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        if (T.level >= 2) {
+            e0 = T.event();
+            e1 = T.event();
+            if (e0) cudaEventRecord(e0, d.stream);
+        }
+        const cudaError_t e = launch_gemm_tc_group(ws, ys, lds, 3, q, EPI_STORE, d.buf.err, d.stream);
+        if (e == cudaSuccess) {
+            count_launch(d);
+            if (T.level >= 1) {
+                T.gemm_launches++;
+                for (int g = 0; g < 3; g++) {
+                    T.gemm_ops += 2.0 * (double)q.M * (double)ws[g]->rows * (double)ws[g]->cols;
+                    T.gemm_bytes += (double)ws[g]->rows * (double)ws[g]->row_bytes + (double)q.M * (double)ws[g]->rows * 4.0;
+                }
+                T.gemm_bytes += (double)q.M * (double)wq.w.cols * 1.125;  // the shared activations, read once
+            }
+            if (e1 && e0) {
+                cudaEventRecord(e1, d.stream);
+                T.gemm.emplace_back(e0, e1);
+            }
+            return;
+        }
+        if (e != cudaErrorNotSupported) check_launch(e, "grouped tensor-core GEMM");
+        if (e0) T.pool.push_back(e0);
+        if (e1) T.pool.push_back(e1);
+    }
+    gemm(C, d, wq, q, yq, ldq, EPI_STORE);
+    gemm(C, d, wk, q, yk, ldkv, EPI_STORE);
+    gemm(C, d, wv, q, yv, ldkv, EPI_STORE);
+}
+
 static QAct qact(Buffers &b, int64_t M, int64_t K) {
     QAct q;
     q.a8 = b.a8;
@@ -658,9 +704,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, an.vec, c.eps, want_norm ? b.ctx : nullptr, qa, s),
                      "attn norm");
         cap(l, SHIELD_ACT_ATTN_NORM, b.ctx, c.hidden);
-        gemm(C, d, wq, qa, b.q, c.qdim(), EPI_STORE);
-        gemm(C, d, wk, qa, b.k, c.kvdim(), EPI_STORE);
-        gemm(C, d, wv, qa, b.v, c.kvdim(), EPI_STORE);
+        gemm_qkv(C, d, wq, wk, wv, qa, b.q, b.k, b.v, c.qdim(), c.kvdim());
         count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
                                  d.temp, b.ctx, s, l == capture_layer && capture_what == SHIELD_ACT_Q_ROPE), "rope q");
         count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,

@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
@@ -263,6 +264,30 @@ __device__ __forceinline__ void unpack_block(const uint8_t *blk, uint32_t (&o)[1
 
 // ------------------------------------------------------------------ kernel
 
+// One launch covers up to GMAX weights that share the activations, the
+// weight type and K (the Q/K/V projections): tiles [tile0[g], tile0[g + 1])
+// belong to weight g, whose outputs go to y[g] (row stride ldy[g]).
+constexpr int GMAX = 3;
+struct TcParams {
+    CUtensorMap a, da, ds;  // activations (f16 integers) and their scales
+    CUtensorMap w[GMAX], b[GMAX], sc[GMAX], off[GMAX];  // raw blocks, f16 copy, scale / offset planes
+    float *y[GMAX];
+    int64_t ldy[GMAX];
+    int64_t tile0[GMAX + 1];
+    int n[GMAX], ntn[GMAX];
+    int count;
+};
+
+// The weight of tile t and the tile's first token and output feature.
+__device__ __forceinline__ int tile_weight(const TcParams &P, int64_t t, int &m0, int &n0) {
+    int g = 0;
+    while (g + 1 < P.count && t >= P.tile0[g + 1]) g++;
+    const int64_t lt = t - P.tile0[g];
+    n0 = (int)(lt % P.ntn[g]) * BN;
+    m0 = (int)(lt / P.ntn[g]) * BM;
+    return g;
+}
+
 // PRE: the weights come pre-unpacked (f16 copy) and their scales from the f32
 // planes, both by TMA; the unpacker warps then idle.
 //
@@ -272,18 +297,13 @@ __device__ __forceinline__ void unpack_block(const uint8_t *blk, uint32_t (&o)[1
 // current tile's epilogue and final stores.
 template <int TYPE, int EPI, bool DOTS, bool PRE>
 __global__ void __launch_bounds__(THREADS, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-          const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_sc,
-          const __grid_constant__ CUtensorMap map_off, const __grid_constant__ CUtensorMap map_da,
-          const __grid_constant__ CUtensorMap map_ds, float *__restrict__ y, int64_t ldy, int M, int N, int nb,
-          int32_t *__restrict__ err, int32_t *__restrict__ dots) {
+k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict__ err, int32_t *__restrict__ dots) {
     using L = Smem<TYPE>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntn = (N + BN - 1) / BN;
-    const int64_t ntiles = (int64_t)ntn * ((M + BM - 1) / BM);
+    const int64_t ntiles = P.tile0[P.count];
 
     uint32_t bar = sbase + L::OFF_BAR;
     // done(s): one tcgen05.commit per block pair, after its four MMAs. Its
@@ -339,7 +359,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             uint32_t pc = 0, cc = 0;  // pairs and chunks issued, over all tiles
             bool ok = true;
             for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
+                int m0, n0;
+                const int gw = tile_weight(P, tile, m0, n0);
                 for (int p = 0; p < npairs; p++, pc++) {
                     if ((2 * p) % CHUNK == 0) {
                         const int c = (2 * p) / CHUNK;
@@ -350,7 +371,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                                 break;
                             }
                             mbar_expect_tx(raw_full(rs), L::RAW_BYTES);
-                            tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &map_w,
+                            tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &P.w[gw],
                                         c * (L::RAW_ROW / 2), n0, raw_full(rs));
                         }
                         if (PRE || !DOTS) {
@@ -362,14 +383,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             const uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
                             mbar_expect_tx(sc_full(ss), (PRE ? L::SC_DA * 4 : 0) + (DOTS ? 0 : L::DA_BYTES));
                             if (PRE) {
-                                tma_load_2d(dst, &map_sc, n0, c * CHUNK, sc_full(ss));
+                                tma_load_2d(dst, &P.sc[gw], n0, c * CHUNK, sc_full(ss));
                                 if (has_offset(TYPE))
-                                    tma_load_2d(dst + CHUNK * BN * 4, &map_off, n0, c * CHUNK, sc_full(ss));
+                                    tma_load_2d(dst + CHUNK * BN * 4, &P.off[gw], n0, c * CHUNK, sc_full(ss));
                             }
                             if (!DOTS) {
-                                tma_load_2d(dst + L::SC_DA * 4, &map_da, c * CHUNK, m0, sc_full(ss));
+                                tma_load_2d(dst + L::SC_DA * 4, &P.da, c * CHUNK, m0, sc_full(ss));
                                 if (has_offset(TYPE))
-                                    tma_load_2d(dst + L::SC_DA * 4 + CHUNK * BM * 4, &map_ds, c * CHUNK, m0,
+                                    tma_load_2d(dst + L::SC_DA * 4 + CHUNK * BM * 4, &P.ds, c * CHUNK, m0,
                                                 sc_full(ss));
                             }
                         }
@@ -381,8 +402,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         break;
                     }
                     mbar_expect_tx(a_full(s), L::A_BYTES + (PRE ? L::B_BYTES : 0));
-                    tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &map_a, 2 * p * 32, m0, a_full(s));
-                    if (PRE) tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &map_b, 2 * p * 32, n0, a_full(s));
+                    tma_load_2d(sbase + L::OFF_A + s * L::A_BYTES, &P.a, 2 * p * 32, m0, a_full(s));
+                    if (PRE) tma_load_2d(sbase + L::OFF_B + s * L::B_BYTES, &P.b[gw], 2 * p * 32, n0, a_full(s));
                 }
             }
         }
@@ -499,7 +520,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         bool ok = true;
         constexpr bool PAIRS = has_offset(TYPE);
         for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-            const int n0 = (int)(tile % ntn) * BN, m0 = (int)(tile / ntn) * BM;
+            int m0, n0;
+            const int gw = tile_weight(P, tile, m0, n0);
+            const int N = P.n[gw];
             const bool warp_live = m0 + q * 32 < M;
             // the accumulators of columns tcol + 8i and tcol + 8i + 1 of token k:
             // f[8k + 2i + e] as scalars, or (offset types, whose two chain steps
@@ -612,7 +635,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 for (int k = 0; k < 4; k++) {
                     const int m = m0 + q * 32 + tr + 8 * k;
                     if (m >= M) continue;
-                    float *dst = y + (int64_t)m * ldy + n0 + tcol;
+                    float *dst = P.y[gw] + (int64_t)m * P.ldy[gw] + n0 + tcol;
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         if (n0 + tcol + 8 * i >= N) break;
@@ -725,41 +748,65 @@ static int sm_count() {
     return cache[dev];
 }
 
+// One weight of a launch: its matrix, where its outputs go and their row stride.
+struct GemmOut {
+    const DevWeight *w;
+    float *y;
+    int64_t ldy;
+};
+
 template <int TYPE, int EPI, bool DOTS, bool PRE>
-static cudaError_t launch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+static cudaError_t launch_t(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
     using L = Smem<TYPE>;
-    CUtensorMap ma, mw, mb, msc, moff, mda, mds;
-    if (!map_activations(&ma, q.a16, q.M, w.cols) || !map_weights(&mw, w, L::RAW_ROW)) return cudaErrorInvalidValue;
-    mb = msc = moff = mda = mds = ma;  // placeholders for the maps a variant never reads
+    if (count < 1 || count > GMAX) return cudaErrorInvalidValue;
+    const int64_t K = outs[0].w->cols;
+    TcParams P;
+    memset(&P, 0, sizeof(P));
+    if (!map_activations(&P.a, q.a16, q.M, K)) return cudaErrorInvalidValue;
+    P.da = P.ds = P.a;  // placeholders for the maps a variant never reads
     if (!DOTS) {
-        if (!map_token_scales(&mda, q.da, q.M, w.cols / 32)) return cudaErrorInvalidValue;
-        if (has_offset(TYPE) && !map_token_scales(&mds, q.ds, q.M, w.cols / 32)) return cudaErrorInvalidValue;
+        if (!map_token_scales(&P.da, q.da, q.M, K / 32)) return cudaErrorInvalidValue;
+        if (has_offset(TYPE) && !map_token_scales(&P.ds, q.ds, q.M, K / 32)) return cudaErrorInvalidValue;
     }
-    if (PRE) {
-        if (!map_activations(&mb, w.w16, w.rows, w.cols) || !map_plane(&msc, w.scale_plane, w.rows, w.cols / 32))
-            return cudaErrorInvalidValue;
-        if (has_offset(TYPE) && !map_plane(&moff, w.offset_plane, w.rows, w.cols / 32)) return cudaErrorInvalidValue;
+    const int64_t ntm = (q.M + BM - 1) / BM;
+    P.count = count;
+    P.tile0[0] = 0;
+    for (int g = 0; g < count; g++) {
+        const DevWeight &w = *outs[g].w;
+        if (w.type != TYPE || w.cols != K) return cudaErrorInvalidValue;
+        if (!map_weights(&P.w[g], w, L::RAW_ROW)) return cudaErrorInvalidValue;
+        P.b[g] = P.sc[g] = P.off[g] = P.w[g];
+        if (PRE) {
+            if (!map_activations(&P.b[g], w.w16, w.rows, w.cols) ||
+                !map_plane(&P.sc[g], w.scale_plane, w.rows, w.cols / 32))
+                return cudaErrorInvalidValue;
+            if (has_offset(TYPE) && !map_plane(&P.off[g], w.offset_plane, w.rows, w.cols / 32))
+                return cudaErrorInvalidValue;
+        }
+        P.y[g] = outs[g].y;
+        P.ldy[g] = outs[g].ldy;
+        P.n[g] = (int)w.rows;
+        P.ntn[g] = (int)((w.rows + BN - 1) / BN);
+        P.tile0[g + 1] = P.tile0[g] + (int64_t)P.ntn[g] * ntm;
     }
     auto kern = k_gemm_tc<TYPE, EPI, DOTS, PRE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return e;
-    const int64_t tiles = ((w.rows + BN - 1) / BN) * ((q.M + BM - 1) / BM);
-    const unsigned grid = (unsigned)std::min<int64_t>(tiles, sm_count());
-    kern<<<grid, THREADS, L::BYTES, s>>>(ma, mw, mb, msc, moff, mda, mds, y, ldy, (int)q.M, (int)w.rows,
-                                         (int)(w.cols / 32), err, dots);
+    const unsigned grid = (unsigned)std::min<int64_t>(P.tile0[count], sm_count());
+    kern<<<grid, THREADS, L::BYTES, s>>>(P, (int)q.M, (int)(K / 32), err, dots);
     return cudaGetLastError();
 }
 
 template <int EPI, bool DOTS, bool PRE>
-static cudaError_t dispatch_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+static cudaError_t dispatch_t(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                               cudaStream_t s) {
-    switch (w.type) {
-    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
-    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
-    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
-    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
-    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS, PRE>(w, q, y, ldy, err, dots, s);
+    switch (outs[0].w->type) {
+    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
+    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
+    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
+    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
+    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -769,12 +816,17 @@ static cudaError_t dispatch_t(const DevWeight &w, const QAct &q, float *y, int64
 constexpr int64_t PRE_MIN_TOKENS = 256;
 static int64_t pre_min_tokens() { return g_pre_min >= 0 ? g_pre_min : PRE_MIN_TOKENS; }
 
+static bool has_copy(const DevWeight &w) {
+    return w.w16 && w.scale_plane && (!has_offset(w.type) || w.offset_plane);
+}
+
 template <int EPI, bool DOTS>
-static cudaError_t dispatch(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int32_t *err, int32_t *dots,
+static cudaError_t dispatch(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
-    if (w.w16 && w.scale_plane && (!has_offset(w.type) || w.offset_plane) && q.M >= pre_min_tokens())
-        return dispatch_t<EPI, DOTS, true>(w, q, y, ldy, err, dots, s);
-    return dispatch_t<EPI, DOTS, false>(w, q, y, ldy, err, dots, s);
+    bool pre = q.M >= pre_min_tokens();
+    for (int g = 0; g < count; g++) pre = pre && has_copy(*outs[g].w);
+    return pre ? dispatch_t<EPI, DOTS, true>(outs, count, q, err, dots, s)
+               : dispatch_t<EPI, DOTS, false>(outs, count, q, err, dots, s);
 }
 
 }  // namespace tc
@@ -790,20 +842,43 @@ bool gemm_tc_supports(const DevWeight &w, int64_t M) {
     return tc::encode_fn() != nullptr;
 }
 
+static bool tc_output_ok(const float *y, int64_t ldy) {
+    return ldy % 4 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+}
+
+static bool tc_activations_ok(const DevWeight &w, const QAct &q) {
+    return q.a16 && reinterpret_cast<uintptr_t>(q.a16) % 16 == 0 && reinterpret_cast<uintptr_t>(q.da) % 16 == 0 &&
+           (!has_offset(w.type) || reinterpret_cast<uintptr_t>(q.ds) % 16 == 0);
+}
+
 cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
                            cudaStream_t s) {
-    if (!gemm_tc_supports(w, q.M) || !q.a16 || ldy % 4 || reinterpret_cast<uintptr_t>(y) % 16 ||
-        reinterpret_cast<uintptr_t>(q.a16) % 16 || reinterpret_cast<uintptr_t>(q.da) % 16 ||
-        (has_offset(w.type) && reinterpret_cast<uintptr_t>(q.ds) % 16))
-        return cudaErrorNotSupported;
+    if (!gemm_tc_supports(w, q.M) || !tc_activations_ok(w, q) || !tc_output_ok(y, ldy)) return cudaErrorNotSupported;
     if (q.M == 0) return cudaSuccess;
-    return epi == EPI_ADD ? tc::dispatch<EPI_ADD, false>(w, q, y, ldy, err, nullptr, s)
-                          : tc::dispatch<EPI_STORE, false>(w, q, y, ldy, err, nullptr, s);
+    const tc::GemmOut out{&w, y, ldy};
+    return epi == EPI_ADD ? tc::dispatch<EPI_ADD, false>(&out, 1, q, err, nullptr, s)
+                          : tc::dispatch<EPI_STORE, false>(&out, 1, q, err, nullptr, s);
+}
+
+cudaError_t launch_gemm_tc_group(const DevWeight *const *ws, float *const *ys, const int64_t *ldys, int count,
+                                 const QAct &q, int epi, int32_t *err, cudaStream_t s) {
+    if (count < 1 || count > tc::GMAX) return cudaErrorNotSupported;
+    tc::GemmOut outs[tc::GMAX];
+    for (int g = 0; g < count; g++) {
+        if (!gemm_tc_supports(*ws[g], q.M) || !tc_activations_ok(*ws[g], q) || !tc_output_ok(ys[g], ldys[g]) ||
+            ws[g]->type != ws[0]->type || ws[g]->cols != ws[0]->cols)
+            return cudaErrorNotSupported;
+        outs[g] = tc::GemmOut{ws[g], ys[g], ldys[g]};
+    }
+    if (q.M == 0) return cudaSuccess;
+    return epi == EPI_ADD ? tc::dispatch<EPI_ADD, false>(outs, count, q, err, nullptr, s)
+                          : tc::dispatch<EPI_STORE, false>(outs, count, q, err, nullptr, s);
 }
 
 cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s) {
     if (!gemm_tc_supports(w, q.M) || !q.a16) return cudaErrorNotSupported;
-    return tc::dispatch<EPI_STORE, true>(w, q, nullptr, 0, err, dots, s);
+    const tc::GemmOut out{&w, nullptr, 0};
+    return tc::dispatch<EPI_STORE, true>(&out, 1, q, err, dots, s);
 }
 
 }  // namespace shield

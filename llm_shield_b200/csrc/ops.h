@@ -72,6 +72,11 @@ cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t
 cudaError_t launch_gemm_tc(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, int32_t *err,
                            cudaStream_t s);
 bool gemm_tc_supports(const DevWeight &w, int64_t M);
+// One launch over up to 3 weights sharing the activations, the weight type and
+// K (the Q/K/V projections): weight g's outputs go to ys[g] with row stride
+// ldys[g]; every output equals the single-weight launch's.
+cudaError_t launch_gemm_tc_group(const DevWeight *const *ws, float *const *ys, const int64_t *ldys, int count,
+                                 const QAct &q, int epi, int32_t *err, cudaStream_t s);
 void gemm_tc_set_pre_min_tokens(int64_t m);
 // Per-block int32 dots (t, n, b) for the bit-exactness check.
 cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s);
