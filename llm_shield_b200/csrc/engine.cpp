@@ -376,18 +376,17 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
     }
 }
 
-// The Q/K/V projections of a layer (same activations): one tensor-core launch
-// covering all three when the kernel takes them (several tiles of each run
-// side by side, which matters when few tokens make few tiles), else one
-// gemm() each. The outputs are identical either way.
-static void gemm_qkv(Ctx &C, Device &d, const Tensor &wq, const Tensor &wk, const Tensor &wv, const QAct &q,
-                     float *yq, float *yk, float *yv, int64_t ldq, int64_t ldkv) {
-    const DevWeight *ws[3] = {&wq.w, &wk.w, &wv.w};
-    float *ys[3] = {yq, yk, yv};
-    const int64_t lds[3] = {ldq, ldkv, ldkv};
+// Projections that share their activations (Q/K/V; gate/up): one
+// tensor-core launch covering all of them when the kernel takes them (the
+// tiles of every weight run side by side, which matters when few tokens make
+// few tiles), else one gemm() each. The outputs are identical either way.
+static void gemm_shared_input(Ctx &C, Device &d, int count, const Tensor *const *W, const QAct &q, float *const *ys,
+                              const int64_t *lds) {
+    const DevWeight *ws[3];
+    for (int g = 0; g < count; g++) ws[g] = &W[g]->w;
     const bool tc_path = C.gemm_path == 0 || C.gemm_path == 2 || C.gemm_path == 3;
-    bool grouped = tc_path && !(C.gemm_path == 0 && gemv_small_supports(wq.w, q.M));
-    for (int g = 0; g < 3 && grouped; g++) grouped = gemm_tc_supports(*ws[g], q.M);
+    bool grouped = count <= 3 && tc_path && !(C.gemm_path == 0 && gemv_small_supports(*ws[0], q.M));
+    for (int g = 0; g < count && grouped; g++) grouped = gemm_tc_supports(*ws[g], q.M);
     if (grouped) {
         Timing &T = d.timing;
         cudaEvent_t e0 = nullptr, e1 = nullptr;
@@ -396,16 +395,16 @@ static void gemm_qkv(Ctx &C, Device &d, const Tensor &wq, const Tensor &wk, cons
             e1 = T.event();
             if (e0) cudaEventRecord(e0, d.stream);
         }
-        const cudaError_t e = launch_gemm_tc_group(ws, ys, lds, 3, q, EPI_STORE, d.buf.err, d.stream);
+        const cudaError_t e = launch_gemm_tc_group(ws, ys, lds, count, q, EPI_STORE, d.buf.err, d.stream);
         if (e == cudaSuccess) {
             count_launch(d);
             if (T.level >= 1) {
                 T.gemm_launches++;
-                for (int g = 0; g < 3; g++) {
+                for (int g = 0; g < count; g++) {
                     T.gemm_ops += 2.0 * (double)q.M * (double)ws[g]->rows * (double)ws[g]->cols;
                     T.gemm_bytes += (double)ws[g]->rows * (double)ws[g]->row_bytes + (double)q.M * (double)ws[g]->rows * 4.0;
                 }
-                T.gemm_bytes += (double)q.M * (double)wq.w.cols * 1.125;  // the shared activations, read once
+                T.gemm_bytes += (double)q.M * (double)ws[0]->cols * 1.125;  // the shared activations, read once
             }
             if (e1 && e0) {
                 cudaEventRecord(e1, d.stream);
@@ -417,9 +416,7 @@ static void gemm_qkv(Ctx &C, Device &d, const Tensor &wq, const Tensor &wk, cons
         if (e0) T.pool.push_back(e0);
         if (e1) T.pool.push_back(e1);
     }
-    gemm(C, d, wq, q, yq, ldq, EPI_STORE);
-    gemm(C, d, wk, q, yk, ldkv, EPI_STORE);
-    gemm(C, d, wv, q, yv, ldkv, EPI_STORE);
+    for (int g = 0; g < count; g++) gemm(C, d, *W[g], q, ys[g], lds[g], EPI_STORE);
 }
 
 static QAct qact(Buffers &b, int64_t M, int64_t K) {
@@ -704,7 +701,12 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, an.vec, c.eps, want_norm ? b.ctx : nullptr, qa, s),
                      "attn norm");
         cap(l, SHIELD_ACT_ATTN_NORM, b.ctx, c.hidden);
-        gemm_qkv(C, d, wq, wk, wv, qa, b.q, b.k, b.v, c.qdim(), c.kvdim());
+        {
+            const Tensor *W[3] = {&wq, &wk, &wv};
+            float *ys[3] = {b.q, b.k, b.v};
+            const int64_t lds[3] = {c.qdim(), c.kvdim(), c.kvdim()};
+            gemm_shared_input(C, d, 3, W, qa, ys, lds);
+        }
         count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
                                  d.temp, b.ctx, s, l == capture_layer && capture_what == SHIELD_ACT_Q_ROPE), "rope q");
         count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
@@ -761,8 +763,12 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         cap(l, SHIELD_ACT_POST_ATTN, b.h, c.hidden);
 
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, nullptr, M, c.hidden, fn.vec, c.eps, nullptr, qa, s), "ffn norm");
-        gemm(C, d, wg, qa, b.g, c.ffn, EPI_STORE);
-        gemm(C, d, wu, qa, b.u, c.ffn, EPI_STORE);
+        {
+            const Tensor *W[2] = {&wg, &wu};
+            float *ys[2] = {b.g, b.u};
+            const int64_t lds[2] = {c.ffn, c.ffn};
+            gemm_shared_input(C, d, 2, W, qa, ys, lds);
+        }
         QAct qf = qact(b, M, c.ffn);
         count_launch(d), check_launch(launch_swiglu_quantize(b.g, b.u, M, c.ffn, qf, s), "swiglu + quantize");
         gemm(C, d, wd, qf, b.h, c.hidden, EPI_ADD);
