@@ -272,6 +272,12 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
  * each other. */
 shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path);
 
+/* Tile width of the tensor-core GEMM: 0 = automatic (64 output features per
+ * tile when 128-wide tiles would leave more than half of the GPU's SMs idle,
+ * i.e. few tokens; else 128), 64 or 128 = that width only. Process-wide; the
+ * outputs are identical at either width. For cross-checking. */
+shield_status shield_set_gemm_tile_width(shield_ctx *ctx, int32_t width);
+
 /* Intermediate tensors of one layer, named as MinistralModel's
  * IActivationSink names them (MinistralModel.cs:212-237). */
 enum {

@@ -1787,6 +1787,14 @@ shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path) {
     });
 }
 
+shield_status shield_set_gemm_tile_width(shield_ctx *ctx, int32_t width) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        if (width != 0 && width != 64 && width != 128) throw Error(SHIELD_ERR_ARG, "width must be 0, 64 or 128");
+        gemm_tc_set_tile_width(width);
+    });
+}
+
 shield_status shield_debug_activation(shield_ctx *ctx, int32_t device, const int32_t *ids, int32_t n, int32_t layer,
                                       int32_t what, float *out) {
     return guarded([&] {

@@ -43,33 +43,33 @@ namespace shield {
 namespace tc {
 
 constexpr int BM = 128;          // tokens per tile (TMEM lanes)
-constexpr int BN = 128;          // output features per tile (TMEM columns per slot)
+constexpr int BN = 128;          // output features per tile (TMEM columns per slot); 64 for small grids
 constexpr int STAGES = 3;        // activation / unpacked-weight stages, 2 blocks each
 constexpr int RAW_STAGES = 2;    // raw weight chunks in flight
 constexpr int SC_STAGES = 2;     // f32 scale chunks in flight
-constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns)
+constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns, or 4 x 64)
 constexpr int CHUNK = 8;         // blocks per raw chunk (TMA inner box = 8 blocks)
 constexpr int EPI_WARPS = 16;              // warp e owns lane quarter e%4 and columns EPI_COLS*(e/4)..
-constexpr int EPI_COLS = BN / (EPI_WARPS / 4);
+template <int TN> constexpr int epi_cols() { return TN / (EPI_WARPS / 4); }  // 32 or 16
 constexpr int THREADS = 128 + 32 * EPI_WARPS;
 constexpr int UNPACK_THREADS = 64;
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int TYPE>
+template <int TYPE, int TN>
 struct Smem {
     static constexpr int BB = block_bytes(TYPE);
     static constexpr int RAW_ROW = CHUNK * BB;   // bytes of one row's chunk
-    static constexpr int RAW_BYTES = BN * RAW_ROW;
+    static constexpr int RAW_BYTES = TN * RAW_ROW;
     static constexpr int A_BYTES = BM * 128;     // 64 f16 per row
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int B_BYTES = TN * 128;
     // one scale stage: weight scales [CHUNK][BN] (+ offsets), then the
     // activation scales [BM][CHUNK] (+ their offset terms)
-    static constexpr int SC_DA = CHUNK * BN * (has_offset(TYPE) ? 2 : 1);
+    static constexpr int SC_DA = CHUNK * TN * (has_offset(TYPE) ? 2 : 1);
     static constexpr int DA_BYTES = CHUNK * BM * 4 * (has_offset(TYPE) ? 2 : 1);
     static constexpr int SC_FLOATS = SC_DA + DA_BYTES / 4;
     static_assert((SC_DA * 4) % 256 == 0 && (SC_FLOATS * 4) % 256 == 0, "swizzled TMA tiles need 256-byte alignment");
-    static_assert(EPI_COLS == 32, "the epilogue's TMEM loads cover 32 columns per warp");
+    static_assert(TN == 128 || TN == 64, "tiles are 128 or 64 features wide");
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
     static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
@@ -167,20 +167,32 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M=128, N=BN.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M=128, N=TN.
+template <int TN>
+constexpr uint32_t idesc() { return (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24); }
 
+template <int TN>
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate));
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "n"(idesc<TN>()), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
+}
+
+// tcgen05.ld 16x256b.x2: the same for 16 columns (registers 0-7).
+__device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
 }
 
 // tcgen05.ld 16x256b.x4: 16 TMEM lanes x 32 columns. Register 4i + e holds
@@ -279,11 +291,12 @@ struct TcParams {
 };
 
 // The weight of tile t and the tile's first token and output feature.
+template <int TN>
 __device__ __forceinline__ int tile_weight(const TcParams &P, int64_t t, int &m0, int &n0) {
     int g = 0;
     while (g + 1 < P.count && t >= P.tile0[g + 1]) g++;
     const int64_t lt = t - P.tile0[g];
-    n0 = (int)(lt % P.ntn[g]) * BN;
+    n0 = (int)(lt % P.ntn[g]) * TN;
     m0 = (int)(lt / P.ntn[g]) * BM;
     return g;
 }
@@ -295,10 +308,10 @@ __device__ __forceinline__ int tile_weight(const TcParams &P, int64_t t, int &m0
 // feature tiles inner) and every ring (operand stages, scale stages, TMEM
 // slots) runs on across tiles, so the next tile's loads and MMAs overlap the
 // current tile's epilogue and final stores.
-template <int TYPE, int EPI, bool DOTS, bool PRE>
+template <int TYPE, int EPI, bool DOTS, bool PRE, int TN>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict__ err, int32_t *__restrict__ dots) {
-    using L = Smem<TYPE>;
+    using L = Smem<TYPE, TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -344,7 +357,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(NSLOT * BN));
+                     "r"(NSLOT * TN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -360,7 +373,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
             bool ok = true;
             for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 int m0, n0;
-                const int gw = tile_weight(P, tile, m0, n0);
+                const int gw = tile_weight<TN>(P, tile, m0, n0);
                 for (int p = 0; p < npairs; p++, pc++) {
                     if ((2 * p) % CHUNK == 0) {
                         const int c = (2 * p) / CHUNK;
@@ -385,7 +398,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                             if (PRE) {
                                 tma_load_2d(dst, &P.sc[gw], n0, c * CHUNK, sc_full(ss));
                                 if (has_offset(TYPE))
-                                    tma_load_2d(dst + CHUNK * BN * 4, &P.off[gw], n0, c * CHUNK, sc_full(ss));
+                                    tma_load_2d(dst + CHUNK * TN * 4, &P.off[gw], n0, c * CHUNK, sc_full(ss));
                             }
                             if (!DOTS) {
                                 tma_load_2d(dst + L::SC_DA * 4, &P.da, c * CHUNK, m0, sc_full(ss));
@@ -436,7 +449,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
 #pragma unroll
                         for (int k = 0; k < 2; k++) {
                             const uint32_t off = (uint32_t)(jb * 64 + 32 * k) >> 4;
-                            umma_f16(tmem_base + (2 * ps + jb) * BN, adesc0 + (uint32_t)(s * L::A_BYTES >> 4) + off,
+                            umma_f16<TN>(tmem_base + (2 * ps + jb) * TN, adesc0 + (uint32_t)(s * L::A_BYTES >> 4) + off,
                                      bdesc0 + (uint32_t)(s * L::B_BYTES >> 4) + off, k);
                         }
                     }
@@ -469,7 +482,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                     }
                     uint8_t *bst = smem + L::OFF_B + s * L::B_BYTES;
 #pragma unroll
-                    for (int rr = 0; rr < 2; rr++) {
+                    for (int rr = 0; rr < TN / 64; rr++) {
                         const int r = ut + rr * 64;
 #pragma unroll
                         for (int jb = 0; jb < 2; jb++) {
@@ -483,9 +496,9 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                                 const uint4 v = make_uint4(o[4 * cq], o[4 * cq + 1], o[4 * cq + 2], o[4 * cq + 3]);
                                 *reinterpret_cast<uint4 *>(bst + r * 128 + ((chunk16 ^ (r & 7)) << 4)) = v;
                             }
-                            sc[j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk));
+                            sc[j * TN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk));
                             if (has_offset(TYPE))
-                                sc[CHUNK * BN + j * BN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
+                                sc[CHUNK * TN + j * TN + r] = h2f(*reinterpret_cast<const uint16_t *>(blk + 2));
                         }
                     }
                     fence_proxy_async();
@@ -504,9 +517,12 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
         // 2 tokens (lane/4 and lane/4 + 8 of a 16-lane half); two loads cover
         // the quarter. A thread so owns 4 tokens x 8 columns and reads each
         // weight scale once for 4 tokens and each token scale once for 8 columns.
+        // (with 64-wide tiles, 16 columns: 2 tokens x 2 columns per load and the
+        // thread's 4 tokens x 4 columns)
+        constexpr int ECOLS = epi_cols<TN>(), NI = ECOLS / 8;
         const int q = warp & 3;
         const int g = (warp - 4) >> 2;
-        const int tr = lane >> 2, tcol = g * EPI_COLS + (lane & 3) * 2;
+        const int tr = lane >> 2, tcol = g * ECOLS + (lane & 3) * 2;
         // byte offsets inside a scale stage: this thread's weight-scale pairs,
         // and its first token's scale row for blocks 0-3 / 4-7 (the 32-byte
         // swizzle moves the row's halves by +-16 bytes when bit 2 of tr is set)
@@ -514,26 +530,26 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
         const uint32_t s16 = ((tr >> 2) & 1) << 4;
         const uint32_t d_off = L::SC_DA * 4 + (uint32_t)(q * 32 + tr) * (CHUNK * 4);
         const uint32_t d_lo = d_off + s16, d_hi = d_off - s16;
-        const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16) + g * EPI_COLS;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16) + g * ECOLS;
         uint32_t cc = 0;               // chunks consumed, over all tiles
         uint32_t dstage = 0, dphase = 0;  // next block pair's commit barrier and parity
         bool ok = true;
         constexpr bool PAIRS = has_offset(TYPE);
         for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             int m0, n0;
-            const int gw = tile_weight(P, tile, m0, n0);
+            const int gw = tile_weight<TN>(P, tile, m0, n0);
             const int N = P.n[gw];
             const bool warp_live = m0 + q * 32 < M;
             // the accumulators of columns tcol + 8i and tcol + 8i + 1 of token k:
             // f[8k + 2i + e] as scalars, or (offset types, whose two chain steps
             // per block pair up better) f2[4k + i] as one f32 pair, each lane of
             // a packed fma being the scalar fma of its output
-            float f[PAIRS ? 1 : 32];
-            uint64_t f2[PAIRS ? 16 : 1];
+            float f[PAIRS ? 1 : 8 * NI];
+            uint64_t f2[PAIRS ? 4 * NI : 1];
 #pragma unroll
-            for (int i = 0; i < (PAIRS ? 1 : 32); i++) f[i] = 0.0f;
+            for (int i = 0; i < (PAIRS ? 1 : 8 * NI); i++) f[i] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < (PAIRS ? 16 : 1); i++) f2[i] = 0;
+            for (int i = 0; i < (PAIRS ? 4 * NI : 1); i++) f2[i] = 0;
             // One chunk of CHUNK blocks. LIVE: the warp's tokens exist (a warp
             // past the last token only keeps the barriers in step). The block
             // loop has no divergent branch: its waits are warp-uniform votes
@@ -554,13 +570,13 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                         tc_fence_after();
                     }
                     if (LIVE) {
-                        uint64_t w2[4], o2[4];
+                        uint64_t w2[NI], o2[NI];
                         float dav[4], dsv[4];
                         if (!DOTS) {
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                w2[i] = lds_b64(w_s + j * BN * 4 + 32 * i);
-                                if (PAIRS) o2[i] = lds_b64(w_s + (CHUNK + j) * BN * 4 + 32 * i);
+                            for (int i = 0; i < NI; i++) {
+                                w2[i] = lds_b64(w_s + j * TN * 4 + 32 * i);
+                                if (PAIRS) o2[i] = lds_b64(w_s + (CHUNK + j) * TN * 4 + 32 * i);
                             }
                             const uint32_t d_s = (j < 4 ? dlo_s : dhi_s) + 4 * j;
 #pragma unroll
@@ -571,15 +587,15 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                         }
 #pragma unroll
                         for (int hh = 0; hh < 2; hh++) {
-                            uint32_t r[16];
-                            tmem_ld16x256(t_lane + ((uint32_t)(16 * hh) << 16) + slot * BN, r);
+                            uint32_t r[4 * NI];
+                            tmem_ld16x256(t_lane + ((uint32_t)(16 * hh) << 16) + slot * TN, r);
                             if (DOTS) {
 #pragma unroll
                                 for (int kk = 0; kk < 2; kk++) {
                                     const int m = m0 + q * 32 + tr + 8 * (2 * hh + kk);
                                     if (m >= M) continue;
 #pragma unroll
-                                    for (int i = 0; i < 4; i++)
+                                    for (int i = 0; i < NI; i++)
 #pragma unroll
                                         for (int e = 0; e < 2; e++) {
                                             const int n = n0 + tcol + 8 * i + e;
@@ -594,14 +610,14 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                                     const int k = 2 * hh + kk;
                                     const uint64_t da2 = pack2u(__float_as_uint(dav[k]), __float_as_uint(dav[k]));
 #pragma unroll
-                                    for (int i = 0; i < 4; i++) {
+                                    for (int i = 0; i < NI; i++) {
                                         // the two scale products as one f32x2 multiply
                                         const uint64_t p2 = mul2(w2[i], da2);
                                         if (PAIRS) {
-                                            f2[4 * k + i] = fma2(pack2u(r[4 * i + 2 * kk], r[4 * i + 2 * kk + 1]),
-                                                                 p2, f2[4 * k + i]);
+                                            f2[NI * k + i] = fma2(pack2u(r[4 * i + 2 * kk], r[4 * i + 2 * kk + 1]),
+                                                                 p2, f2[NI * k + i]);
                                         } else {
-                                            float *fk = f + 8 * k + 2 * i;
+                                            float *fk = f + 2 * NI * k + 2 * i;
                                             fk[0] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk]), lo_f(p2), fk[0]);
                                             fk[1] = __fmaf_rn(__uint_as_float(r[4 * i + 2 * kk + 1]), hi_f(p2),
                                                               fk[1]);
@@ -610,7 +626,7 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                                     if (PAIRS) {
                                         const uint64_t ds2 = pack2u(__float_as_uint(dsv[k]), __float_as_uint(dsv[k]));
 #pragma unroll
-                                        for (int i = 0; i < 4; i++) f2[4 * k + i] = fma2(o2[i], ds2, f2[4 * k + i]);
+                                        for (int i = 0; i < NI; i++) f2[NI * k + i] = fma2(o2[i], ds2, f2[NI * k + i]);
                                     }
                                 }
                             }
@@ -637,10 +653,10 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                     if (m >= M) continue;
                     float *dst = P.y[gw] + (int64_t)m * P.ldy[gw] + n0 + tcol;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
+                    for (int i = 0; i < NI; i++) {
                         if (n0 + tcol + 8 * i >= N) break;
-                        float2 v = PAIRS ? make_float2(lo_f(f2[4 * k + i]), hi_f(f2[4 * k + i]))
-                                         : make_float2(f[8 * k + 2 * i], f[8 * k + 2 * i + 1]);
+                        float2 v = PAIRS ? make_float2(lo_f(f2[NI * k + i]), hi_f(f2[NI * k + i]))
+                                         : make_float2(f[2 * NI * k + 2 * i], f[2 * NI * k + 2 * i + 1]);
                         if (EPI == EPI_ADD) {
                             const float2 o = *reinterpret_cast<const float2 *>(dst + 8 * i);
                             v.x = __fadd_rn(o.x, v.x);
@@ -658,13 +674,14 @@ done:
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(NSLOT * BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(NSLOT * TN));
     }
 }
 
 // ------------------------------------------------------------------ host
 
 static int64_t g_pre_min = -1;
+static int g_tile_width = 0;  // 0: by the grid size; 64 or 128: forced
 static int64_t pre_min_tokens();
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -680,12 +697,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Activations: f16 [M][K], box 64 x 128 rows, 128B swizzle.
-static bool map_activations(CUtensorMap *m, const __half *a, int64_t M, int64_t K) {
+static bool map_activations(CUtensorMap *m, const __half *a, int64_t M, int64_t K, int box_rows = BM) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-    cuuint32_t box[2] = {64, BM};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)a, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -693,12 +710,12 @@ static bool map_activations(CUtensorMap *m, const __half *a, int64_t M, int64_t 
 }
 
 // Raw weights: rows of 16-bit units, box = one 8-block chunk x 128 rows.
-static bool map_weights(CUtensorMap *m, const DevWeight &w, int raw_row) {
+static bool map_weights(CUtensorMap *m, const DevWeight &w, int raw_row, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)(w.row_bytes / 2), (cuuint64_t)w.rows};
     cuuint64_t strides[1] = {(cuuint64_t)w.row_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)(raw_row / 2), BN};
+    cuuint32_t box[2] = {(cuuint32_t)(raw_row / 2), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)w.data, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -706,12 +723,12 @@ static bool map_weights(CUtensorMap *m, const DevWeight &w, int raw_row) {
 }
 
 // f32 scale (or offset) plane [K/32][rows], box = 128 features x 8 blocks.
-static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t nb) {
+static bool map_plane(CUtensorMap *m, const float *plane, int64_t rows, int64_t nb, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)rows, (cuuint64_t)nb};
     cuuint64_t strides[1] = {(cuuint64_t)(rows * 4)};
-    cuuint32_t box[2] = {BN, CHUNK};
+    cuuint32_t box[2] = {(cuuint32_t)box_rows, CHUNK};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)plane, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -755,10 +772,10 @@ struct GemmOut {
     int64_t ldy;
 };
 
-template <int TYPE, int EPI, bool DOTS, bool PRE>
+template <int TYPE, int EPI, bool DOTS, bool PRE, int TN>
 static cudaError_t launch_t(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
-    using L = Smem<TYPE>;
+    using L = Smem<TYPE, TN>;
     if (count < 1 || count > GMAX) return cudaErrorInvalidValue;
     const int64_t K = outs[0].w->cols;
     TcParams P;
@@ -775,22 +792,22 @@ static cudaError_t launch_t(const GemmOut *outs, int count, const QAct &q, int32
     for (int g = 0; g < count; g++) {
         const DevWeight &w = *outs[g].w;
         if (w.type != TYPE || w.cols != K) return cudaErrorInvalidValue;
-        if (!map_weights(&P.w[g], w, L::RAW_ROW)) return cudaErrorInvalidValue;
+        if (!map_weights(&P.w[g], w, L::RAW_ROW, TN)) return cudaErrorInvalidValue;
         P.b[g] = P.sc[g] = P.off[g] = P.w[g];
         if (PRE) {
-            if (!map_activations(&P.b[g], w.w16, w.rows, w.cols) ||
-                !map_plane(&P.sc[g], w.scale_plane, w.rows, w.cols / 32))
+            if (!map_activations(&P.b[g], w.w16, w.rows, w.cols, TN) ||
+                !map_plane(&P.sc[g], w.scale_plane, w.rows, w.cols / 32, TN))
                 return cudaErrorInvalidValue;
-            if (has_offset(TYPE) && !map_plane(&P.off[g], w.offset_plane, w.rows, w.cols / 32))
+            if (has_offset(TYPE) && !map_plane(&P.off[g], w.offset_plane, w.rows, w.cols / 32, TN))
                 return cudaErrorInvalidValue;
         }
         P.y[g] = outs[g].y;
         P.ldy[g] = outs[g].ldy;
         P.n[g] = (int)w.rows;
-        P.ntn[g] = (int)((w.rows + BN - 1) / BN);
+        P.ntn[g] = (int)((w.rows + TN - 1) / TN);
         P.tile0[g + 1] = P.tile0[g] + (int64_t)P.ntn[g] * ntm;
     }
-    auto kern = k_gemm_tc<TYPE, EPI, DOTS, PRE>;
+    auto kern = k_gemm_tc<TYPE, EPI, DOTS, PRE, TN>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return e;
     const unsigned grid = (unsigned)std::min<int64_t>(P.tile0[count], sm_count());
@@ -798,15 +815,15 @@ static cudaError_t launch_t(const GemmOut *outs, int count, const QAct &q, int32
     return cudaGetLastError();
 }
 
-template <int EPI, bool DOTS, bool PRE>
+template <int EPI, bool DOTS, bool PRE, int TN>
 static cudaError_t dispatch_t(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                               cudaStream_t s) {
     switch (outs[0].w->type) {
-    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
-    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
-    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
-    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
-    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS, PRE>(outs, count, q, err, dots, s);
+    case T_Q4_0: return launch_t<T_Q4_0, EPI, DOTS, PRE, TN>(outs, count, q, err, dots, s);
+    case T_Q4_1: return launch_t<T_Q4_1, EPI, DOTS, PRE, TN>(outs, count, q, err, dots, s);
+    case T_Q5_0: return launch_t<T_Q5_0, EPI, DOTS, PRE, TN>(outs, count, q, err, dots, s);
+    case T_Q5_1: return launch_t<T_Q5_1, EPI, DOTS, PRE, TN>(outs, count, q, err, dots, s);
+    case T_Q8_0: return launch_t<T_Q8_0, EPI, DOTS, PRE, TN>(outs, count, q, err, dots, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -820,13 +837,25 @@ static bool has_copy(const DevWeight &w) {
     return w.w16 && w.scale_plane && (!has_offset(w.type) || w.offset_plane);
 }
 
+// 64-wide tiles when 128-wide ones would leave more than half of the SMs
+// idle (few tokens): twice the tiles, half the epilogue work per block.
+static bool narrow_tiles(const GemmOut *outs, int count, const QAct &q) {
+    int64_t tiles = 0;
+    for (int g = 0; g < count; g++) tiles += (outs[g].w->rows + BN - 1) / BN;
+    tiles *= (q.M + BM - 1) / BM;
+    return g_tile_width != 128 && (g_tile_width == 64 || 2 * tiles <= sm_count());
+}
+
 template <int EPI, bool DOTS>
 static cudaError_t dispatch(const GemmOut *outs, int count, const QAct &q, int32_t *err, int32_t *dots,
                             cudaStream_t s) {
     bool pre = q.M >= pre_min_tokens();
     for (int g = 0; g < count; g++) pre = pre && has_copy(*outs[g].w);
-    return pre ? dispatch_t<EPI, DOTS, true>(outs, count, q, err, dots, s)
-               : dispatch_t<EPI, DOTS, false>(outs, count, q, err, dots, s);
+    if (!DOTS && narrow_tiles(outs, count, q))
+        return pre ? dispatch_t<EPI, DOTS, true, 64>(outs, count, q, err, dots, s)
+                   : dispatch_t<EPI, DOTS, false, 64>(outs, count, q, err, dots, s);
+    return pre ? dispatch_t<EPI, DOTS, true, 128>(outs, count, q, err, dots, s)
+               : dispatch_t<EPI, DOTS, false, 128>(outs, count, q, err, dots, s);
 }
 
 }  // namespace tc
@@ -834,6 +863,10 @@ static cudaError_t dispatch(const GemmOut *outs, int count, const QAct &q, int32
 // Token count from which the tensor-core GEMM reads the pre-unpacked weights
 // (negative: the built-in default). Used by tests to cover both paths.
 void gemm_tc_set_pre_min_tokens(int64_t m) { tc::g_pre_min = m; }
+
+// Tile width of the tensor-core GEMM: 0 chooses by the grid size, 64 or 128
+// forces it (tests cover both).
+void gemm_tc_set_tile_width(int w) { tc::g_tile_width = w; }
 
 bool gemm_tc_supports(const DevWeight &w, int64_t M) {
     if (!block_bytes(w.type) || w.cols % 256 || w.rows % 16 || M < 1 || M > (1LL << 31) - 1) return false;

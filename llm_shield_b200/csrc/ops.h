@@ -78,6 +78,7 @@ bool gemm_tc_supports(const DevWeight &w, int64_t M);
 cudaError_t launch_gemm_tc_group(const DevWeight *const *ws, float *const *ys, const int64_t *ldys, int count,
                                  const QAct &q, int epi, int32_t *err, cudaStream_t s);
 void gemm_tc_set_pre_min_tokens(int64_t m);
+void gemm_tc_set_tile_width(int w);
 // Per-block int32 dots (t, n, b) for the bit-exactness check.
 cudaError_t launch_block_dots(const DevWeight &w, const QAct &q, int32_t *dots, cudaStream_t s);
 cudaError_t launch_block_dots_tc(const DevWeight &w, const QAct &q, int32_t *dots, int32_t *err, cudaStream_t s);

@@ -166,3 +166,25 @@ def test_sweep_shapes_at_prefill_sizes_match_oracle(ctx, qtype, rows, cols):
                                               err_msg="raw blocks, M=512")
             finally:
                 ctx.set_gemm_path(0)
+
+
+@pytest.mark.parametrize("qtype", INT_TYPES)
+@pytest.mark.parametrize("width", [64, 128])
+def test_tile_widths_bit_identical_to_oracle(ctx, qtype, width):
+    """The tensor-core GEMM's 64- and 128-wide tiles (64 is chosen
+    automatically when 128-wide tiles would leave most SMs idle), on both its
+    weight paths, against the oracle; rows that end in a partial tile."""
+    rows, cols = 400, 768
+    w = random_weights(qtype, rows, cols, seed=11 * width + qtype)
+    upload(ctx, "blk.0.attn_output.weight", qtype, rows, cols, w)
+    try:
+        ctx.set_gemm_tile_width(width)
+        for path, tokens in ((2, 130), (3, 300)):
+            x = np.random.default_rng(tokens + width).uniform(-1, 1, (tokens, cols)).astype(np.float32)
+            ctx.set_gemm_path(path)
+            got = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows)
+            np.testing.assert_array_equal(got, oracle.qmatmul(qtype, w, rows, cols, x, tokens),
+                                          err_msg=f"path {path}, {tokens} tokens")
+    finally:
+        ctx.set_gemm_path(0)
+        ctx.set_gemm_tile_width(0)
