@@ -221,6 +221,7 @@ struct Timing {
 
 struct Device {
     int ordinal = 0;
+    int sms = 148;  // streaming multiprocessors
     cudaStream_t stream = nullptr;
     Timing timing;
     std::unordered_map<std::string, Tensor> tensors;
@@ -459,7 +460,7 @@ static void ensure_buffers(Ctx &C, Device &d) {
     SHIELD_CUDA(cudaMallocHost((void **)&d.buf.h_logits, (size_t)(T * 64) * 4));
     // attention scratch: at least one work item of the longest request, at
     // most 4 GiB (a micro-batch needing more is attended in several launches)
-    int64_t one = attention_scratch_floats(c.max_positions, c.n_kv_heads);
+    int64_t one = attention_scratch_floats(c.max_positions, c.n_kv_heads, attention_rows_per_cta());
     int64_t all = std::min<int64_t>((int64_t)1 << 30, (int64_t)c.n_heads * T * c.max_positions);
     d.buf.scores_cap = std::max(one, all);
     dev_alloc(d.buf.scores, (size_t)d.buf.scores_cap);
@@ -548,7 +549,16 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     // attention: one work item per (request, 128/G query tokens), longest
     // first (the CTAs of long rows start early instead of forming a tail), in
     // groups whose scratch fits the buffer
-    const int G = c.n_heads / c.n_kv_heads, QT = attention_rows_per_cta() / G;
+    // 64 query rows per CTA instead of 128 when 128-row items would give fewer
+    // than two CTAs per SM (small batches: a single short request)
+    const int G = c.n_heads / c.n_kv_heads;
+    int att_rows = attention_rows_per_cta();
+    {
+        int64_t n128 = 0;
+        for (int r = 0; r < R; r++) n128 += (B.len[r] + att_rows / G - 1) / (att_rows / G);
+        if (n128 * c.n_kv_heads < 2 * (int64_t)d.sms && (att_rows / 2) % G == 0) att_rows /= 2;
+    }
+    const int QT = att_rows / G;
     struct AttGroup { int w0, nw; };
     struct AttItem { int64_t kend; int32_t r, q0; };
     std::vector<AttItem> items;
@@ -563,7 +573,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         int64_t used = 0;
         AttGroup cur{0, 0};
         for (const AttItem &it : items) {
-            const int64_t need = attention_scratch_floats(it.kend, c.n_kv_heads);
+            const int64_t need = attention_scratch_floats(it.kend, c.n_kv_heads, att_rows);
             if (used + need > b.scores_cap && cur.nw > 0) {
                 groups.push_back(cur);
                 cur = AttGroup{(int)wbase.size(), 0};
@@ -622,6 +632,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     const int saved_level = T.level;
     if (graph) {
         std::string key = std::to_string(M) + "/" + std::to_string(R) + "/" + std::to_string(nv) + "/" +
+                          std::to_string(att_rows) + "/" +
                           (full_logits ? "f" : "-") + (any_append ? "a" : "-");
         for (const AttGroup &ag : groups) key += "/" + std::to_string(ag.w0) + ":" + std::to_string(ag.nw);
         auto it = d.graphs.find(key);
@@ -749,7 +760,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             d.timing.launches += 1;
             A.work = d_work + ag.w0;
             A.work_base = d_wbase + ag.w0;
-            check_launch(launch_attention(A, ag.nw, c.head_dim, s), "attention");
+            check_launch(launch_attention(A, ag.nw, c.head_dim, att_rows, s), "attention");
         }
         if (a0 && a1) {
             cudaEventRecord(a1, s);
@@ -1565,6 +1576,7 @@ shield_status shield_open(int32_t device_mask, shield_ctx **out) {
             auto d = std::make_unique<Device>();
             d->ordinal = i;
             SHIELD_CUDA(cudaSetDevice(i));
+            SHIELD_CUDA(cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, i));
             SHIELD_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
             ctx->c.devs.push_back(std::move(d));
         }

@@ -167,6 +167,7 @@ struct AttView {
     const float *ck, *cv;          // this layer's cached keys and values (pre > 0)
 };
 
+template <int RR>
 __device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
     const int2 wk = A.work[blockIdx.x];
     AttView w;
@@ -178,7 +179,7 @@ __device__ __forceinline__ AttView att_view(const AttArgs &A, int QT) {
     w.qend = min(w.q0 + QT, w.len);
     w.kend = w.pre + w.qend;
     w.ld = att_ld(w.kend);
-    w.sc = A.scores + A.work_base[blockIdx.x] + (int64_t)blockIdx.y * att::R * w.ld;
+    w.sc = A.scores + A.work_base[blockIdx.x] + (int64_t)blockIdx.y * RR * w.ld;
     w.ck = w.cv = nullptr;
     if (w.pre > 0) {
         const int64_t off = (int64_t)A.layer * A.cache_stride[r];
@@ -198,8 +199,10 @@ __device__ __forceinline__ const float *kv_row(const float *own, const float *ca
 // maximum into rowmax[] (shared). Keys and the CTA's query rows arrive in
 // chain-major order (see chain_pos) by cp.async, key tiles double-buffered.
 // Thread (warp, rl, kl) owns rows warp*16 + rl + 4a and keys kl + 8b of a tile.
+template <int RR>
 __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, float *sm, float *rowmax) {
     using namespace att;
+    constexpr int R = RR, THREADS = 2 * RR;  // rows of the CTA, its threads
     float *Qs = sm;  // R x LD, then two KT x LD key tiles
     const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
@@ -310,8 +313,10 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
 // Phase 2: one warp per row, rows warp, warp + 8, ..: e = exp(s - max) in
 // place summed as 32 lane-strided partials, then w = e / sum in place; a row
 // whose maximum is not finite becomes uniform (Kernels.Softmax).
+template <int RR>
 __device__ __forceinline__ void attn_softmax(const AttArgs &A, const AttView &w, const float *rowmax) {
     using namespace att;
+    constexpr int R = RR, THREADS = 2 * RR;
     const int G = A.n_heads / A.n_kv_heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int row = warp; row < R; row += THREADS / 32) {
@@ -366,8 +371,10 @@ __device__ __forceinline__ void attn_softmax(const AttArgs &A, const AttView &w,
 // exp values are double-buffered in shared memory by cp.async; each weight
 // tile is divided once in place (masked keys to 0) before use. Thread (tr, td)
 // owns rows tr + 32a and dims td*4 + 32e (a, e < 4).
+template <int RR>
 __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, float *sm) {
     using namespace att;
+    constexpr int R = RR, THREADS = 2 * RR, RSTEP = THREADS / 8;  // thread (tr, td) owns rows tr + RSTEP*a
     constexpr int V_FLOATS = PKT * LD, W_FLOATS = R * LDP;
     const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
@@ -428,7 +435,7 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
         for (; kk + 4 <= kn; kk += 4) {
             float4 wt[4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + 32 * a) * LDP + kk]);
+            for (int a = 0; a < 4; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + RSTEP * a) * LDP + kk]);
             key(vs + (uint32_t)((kk + 0) * LD) * 4, {wt[0].x, wt[1].x, wt[2].x, wt[3].x});
             key(vs + (uint32_t)((kk + 1) * LD) * 4, {wt[0].y, wt[1].y, wt[2].y, wt[3].y});
             key(vs + (uint32_t)((kk + 2) * LD) * 4, {wt[0].z, wt[1].z, wt[2].z, wt[3].z});
@@ -437,14 +444,14 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
         for (; kk < kn; kk++) {
             float wa[4];
 #pragma unroll
-            for (int a = 0; a < 4; a++) wa[a] = W[(tr + 32 * a) * LDP + kk];
+            for (int a = 0; a < 4; a++) wa[a] = W[(tr + RSTEP * a) * LDP + kk];
             key(vs + (uint32_t)(kk * LD) * 4, wa);
         }
         __syncthreads();
     }
 #pragma unroll
     for (int a = 0; a < 4; a++) {
-        const int row = tr + 32 * a, i = row / G, g = row % G, tok = w.q0 + i;
+        const int row = tr + RSTEP * a, i = row / G, g = row % G, tok = w.q0 + i;
         if (tok >= w.len) continue;
         float *dst = A.ctx + (w.start + tok) * qdim + (int64_t)(h * G + g) * HD;
 #pragma unroll
@@ -454,26 +461,38 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
     }
 }
 
-__global__ void __launch_bounds__(att::THREADS, 2) k_attn(const AttArgs A) {
+// RR query rows per CTA with 2 x RR threads: 128 for large batches, 64 for
+// small ones (twice the CTAs when few work items would leave SMs idle).
+template <int RR>
+__global__ void __launch_bounds__(2 * RR, RR == 128 ? 2 : 3) k_attn(const AttArgs A) {
     extern __shared__ float sm[];
-    __shared__ float rowmax[att::R];
-    const AttView w = att_view(A, att::R / (A.n_heads / A.n_kv_heads));
-    attn_scores(A, w, sm, rowmax);
+    __shared__ float rowmax[RR];
+    const AttView w = att_view<RR>(A, RR / (A.n_heads / A.n_kv_heads));
+    attn_scores<RR>(A, w, sm, rowmax);
     __syncthreads();
-    attn_softmax(A, w, rowmax);
+    attn_softmax<RR>(A, w, rowmax);
     __syncthreads();
-    attn_pv(A, w, sm);
+    attn_pv<RR>(A, w, sm);
 }
 
-cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, cudaStream_t s) {
+template <int RR>
+static cudaError_t launch_attn_rows(const AttArgs &A, int n_work, cudaStream_t s) {
+    using namespace att;
+    if (RR % (A.n_heads / A.n_kv_heads)) return cudaErrorInvalidValue;
+    const size_t smem = std::max((size_t)(RR + 2 * KT) * LD * 4, (size_t)2 * (PKT * LD + RR * LDP) * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_attn<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_attn<RR><<<dim3((unsigned)n_work, (unsigned)A.n_kv_heads), 2 * RR, smem, s>>>(A);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, int rows, cudaStream_t s) {
     using namespace att;
     if (n_work == 0) return cudaSuccess;
-    if (head_dim != HD || A.n_heads % A.n_kv_heads || R % (A.n_heads / A.n_kv_heads)) return cudaErrorInvalidValue;
-    const size_t smem = std::max((size_t)(R + 2 * KT) * LD * 4, (size_t)2 * (PKT * LD + R * LDP) * 4);
-    cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_attn<<<dim3((unsigned)n_work, (unsigned)A.n_kv_heads), THREADS, smem, s>>>(A);
-    return cudaGetLastError();
+    if (head_dim != HD || A.n_heads % A.n_kv_heads) return cudaErrorInvalidValue;
+    if (rows == 128) return launch_attn_rows<128>(A, n_work, s);
+    if (rows == 64) return launch_attn_rows<64>(A, n_work, s);
+    return cudaErrorInvalidValue;
 }
 
 int attention_rows_per_cta() { return att::R; }

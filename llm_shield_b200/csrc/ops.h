@@ -97,10 +97,11 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
                         cudaStream_t s, bool natural = true);
 // Causal GQA attention of a group of work items (one fused kernel, see
 // forward_ops.cu). work[i] = {request, first query token}; one CTA per (work
-// item, KV head) covers attention_rows_per_cta() query rows (tokens x the
-// heads of a group). Its scores live in the scratch while it runs:
-// attention_scratch_floats(kend) floats per work item from work_base[i],
-// kend = pre + the last query token + 1, the KV heads' rows one after another.
+// item, KV head) covers `rows` query rows (rows / G tokens x the G heads of a
+// group; rows is attention_rows_per_cta(), or half of it for small batches).
+// Its scores live in the scratch while it runs: attention_scratch_floats(kend,
+// n_kv_heads, rows) floats per work item from work_base[i], kend = pre + the
+// last query token + 1, the KV heads' rows one after another.
 struct AttArgs {
     const float *qc = nullptr;      // queries after RoPE, chain-major (launch_rope's perm output)
     const float *kc = nullptr;      // keys after RoPE, chain-major
@@ -120,7 +121,9 @@ struct AttArgs {
     int n_heads = 0, n_kv_heads = 0;
     float scale = 0.0f;
 };
-cudaError_t launch_attention(const AttArgs &args, int n_work, int head_dim, cudaStream_t s);
+// rows: query rows per CTA, 128 or 64 (the work list's tokens per item are
+// rows / the GQA group).
+cudaError_t launch_attention(const AttArgs &args, int n_work, int head_dim, int rows, cudaStream_t s);
 // Appends the batch's new keys (chain-major) and values of one layer to the
 // caches of the requests with a non-null append[r]: rows req_start[r] + t go
 // to position req_pre[r] + t of that cache (KvCache.Append, KvCache.cs).
@@ -133,9 +136,10 @@ cudaError_t launch_append_kv(const AttArgs &args, const uint8_t *append, int n_r
 cudaError_t launch_prefix_state(float *dev_k, float *dev_v, float *snap_k, float *snap_v, int64_t P, int kv_heads,
                                 int head_dim, bool to_device, cudaStream_t s);
 int attention_rows_per_cta();
-// Scratch floats of one work item whose rows attend to kend keys, all KV heads.
-inline int64_t attention_scratch_floats(int64_t kend, int n_kv_heads) {
-    return (int64_t)n_kv_heads * attention_rows_per_cta() * ((kend + 3) & ~int64_t(3));
+// Scratch floats of one work item of `rows` query rows attending to kend keys,
+// all KV heads.
+inline int64_t attention_scratch_floats(int64_t kend, int n_kv_heads, int rows) {
+    return (int64_t)n_kv_heads * rows * ((kend + 3) & ~int64_t(3));
 }
 
 }  // namespace shield
