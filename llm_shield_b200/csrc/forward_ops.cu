@@ -137,7 +137,8 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 // Causal grouped-query attention over a ragged batch (AttendGroup,
 // MinistralModel.cs:372-440) in one kernel that keeps the oracle's exact
 // operation order, so the context is bit-identical to it. One CTA owns 128
-// query rows of one request and one KV head: 128/G tokens x the G query heads
+// query rows (64 for small batches, which then get twice the CTAs) of one
+// request and one KV head: 128/G tokens x the G query heads
 // sharing that KV head, so each key and value row is read once per CTA for all
 // of them. A request's queries are its tokens in the batch; its keys are the
 // first pre positions of its cache (the system-prompt cache of

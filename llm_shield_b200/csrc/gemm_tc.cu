@@ -5,7 +5,9 @@
 // per-output operation sequence as the reference and the oracle, so outputs
 // are bit-identical to theirs.
 //
-// Tile: 128 tokens (TMEM lanes / UMMA M) x 128 output features (UMMA N).
+// Tile: 128 tokens (TMEM lanes / UMMA M) x 128 output features (UMMA N), or
+// x 64 when 128-wide tiles would leave most SMs idle (few tokens). One launch
+// can cover up to three weights that share the activations (Q/K/V, gate/up).
 // Per 32-element quant block the tile needs its own int32 result, because the
 // f32 chain scales every block separately; one block is one UMMA K-step.
 //
@@ -18,7 +20,7 @@
 //   warps 2-3   unpack raw blocks in registers (nibbles, 5th bits, Q8 bytes) to
 //               f16 integers in the canonical SW128 K-major layout; widen the
 //               f16 block scales (and offsets) to f32
-//   warps 4-19  epilogue, 32 output features each: tcgen05.ld the slot, apply
+//   warps 4-19  epilogue, 32 (or 16) output features each: tcgen05.ld the slot, apply
 //               the block's f32 scaling chain per output (packed f32x2
 //               operations), write or add to y
 //
