@@ -13,7 +13,7 @@ constexpr int R = 128;       // query rows per CTA
 constexpr int HD = 128;      // head_dim this kernel is written for
 constexpr int KT = 32;       // keys per tile
 constexpr int LD = HD + 4;   // padded row of a Q/K/V tile in shared memory
-constexpr int THREADS = 256;
+constexpr int THREADS = 256;  // threads of a 128-row CTA (2 per row)
 constexpr int PKT = 32;      // keys per PV tile
 constexpr int LDP = PKT + 4; // padded row of a PV weight tile
 }  // namespace att
