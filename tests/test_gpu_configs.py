@@ -116,3 +116,19 @@ def test_attention_temperature_past_the_training_window(shield_lib):
         np.testing.assert_array_equal(plain[2], out[3][2])
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("qtype,length", [(synth.Q8_0, 4096), (synth.Q5_1, 1024), (synth.Q4_0, 2048)],
+                         ids=["config4-Q8_0-4096", "config3-Q5_1-1024", "config5-Q4_0-2048"])
+def test_full_depth_long_request_matches_the_oracle(shield_lib, qtype, length):
+    """The longest requests of configs 4, 3 and 5 through all 26 layers of the
+    3B model, bit for bit against the oracle (each takes the oracle one to two
+    minutes on the host cores), inside a batch with a short request."""
+    spec = dataclasses.replace(synth.SHIELDSTRAL_3B, qtype=qtype)
+    tensors, ctx = _model(spec, 4096, 16384)
+    try:
+        reqs = synth.random_requests(2, [length, 48], seed=1000 + qtype, vocab=spec.vocab)
+        out = ctx.score_batch(reqs, spec.verdict_ids, len(spec.yes_ids))
+        _check_exact(oracle_model(spec, tensors), spec, reqs, *out, which=(0,))
+    finally:
+        ctx.close()
