@@ -12,14 +12,15 @@
 // f32 chain scales every block separately; one block is one UMMA K-step.
 //
 //   warp 0      TMA producer: activation tiles (f16 holding the int8 values,
-//               128B-swizzled K-major) and raw GGUF weight chunks (8 blocks per
-//               row, bytes unchanged)
+//               128B-swizzled K-major) and either the weights' once-unpacked
+//               f16 copy (same layout; every layer matrix has one) or raw GGUF
+//               weight chunks (8 blocks per row, bytes unchanged)
 //   warp 1      TMEM owner + MMA issuer: two tcgen05.mma.kind::f16 (K=16) per
 //               block into one of four 128-column TMEM slots, one commit per
 //               block pair
-//   warps 2-3   unpack raw blocks in registers (nibbles, 5th bits, Q8 bytes) to
-//               f16 integers in the canonical SW128 K-major layout; widen the
-//               f16 block scales (and offsets) to f32
+//   warps 2-3   raw-chunk path only: unpack raw blocks in registers (nibbles,
+//               5th bits, Q8 bytes) to f16 integers in the canonical SW128
+//               K-major layout; widen the f16 block scales (and offsets) to f32
 //   warps 4-19  epilogue, 32 (or 16) output features each: tcgen05.ld the slot, apply
 //               the block's f32 scaling chain per output (packed f32x2
 //               operations), write or add to y
@@ -830,9 +831,11 @@ static cudaError_t dispatch_t(const GemmOut *outs, int count, const QAct &q, int
     }
 }
 
-// Long token batches read the pre-unpacked copy (every 128-token tile would
-// otherwise unpack the same weights again); short ones stream the raw blocks.
-constexpr int64_t PRE_MIN_TOKENS = 256;
+// Every token batch reads the pre-unpacked copy when the weight has one: on
+// the raw blocks each 128-token tile unpacks the whole weight again, and two
+// unpacker warps cannot keep up even at 17-255 tokens (the copy is 1.1-2.4x
+// faster there). The raw-block kernel serves weights without a copy.
+constexpr int64_t PRE_MIN_TOKENS = 1;
 static int64_t pre_min_tokens() { return g_pre_min >= 0 ? g_pre_min : PRE_MIN_TOKENS; }
 
 static bool has_copy(const DevWeight &w) {

@@ -43,10 +43,10 @@ def _run(ctx, torch, name, x, rows, noalloc):
     return dy.cpu().numpy()
 
 
-# (type, rows, cols, M, weight name): the tensor-core kernel on the raw blocks
-# (M = 200), on the once-unpacked layer copy (M = 600 at K = 3072, just under
-# the scratch limit), the few-token kernel (M = 5), and the CUDA-core kernel
-# (K = 256 has no tensor-core tile)
+# (type, rows, cols, M, weight name): the tensor-core kernel on the
+# once-unpacked layer copy (M = 200, and M = 600 at K = 3072, just under the
+# scratch limit), the few-token kernel (M = 5), and the CUDA-core kernel
+# (K = 256 has no tensor-core tile); the raw-block kernel is checked below
 CASES = [(synth.Q4_0, 256, 3072, 200, "blk.0.attn_q.weight"),
          (synth.Q5_1, 100, 256, 13, "blk.0.attn_k.weight"),
          (synth.Q4_0, 512, 3072, 600, "blk.0.ffn_gate.weight"),
@@ -90,11 +90,20 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
 
 
 def test_noalloc_follows_the_selected_kernel(ctx):
-    """shield_set_gemm_path applies here too: the few-token kernel alone
+    """shield_set_gemm_path applies here too: the raw-block tensor-core kernel
+    (path 2) gives the oracle's outputs, and the few-token kernel alone
     (path 4) refuses 17 tokens, as the allocating entry points do."""
     torch = pytest.importorskip("torch")
     rows, cols = 128, 3072
-    ctx.upload("blk.0.attn_output.weight", synth.Q4_0, rows, cols, random_weights(synth.Q4_0, rows, cols, seed=9))
+    w = random_weights(synth.Q4_0, rows, cols, seed=9)
+    ctx.upload("blk.0.attn_output.weight", synth.Q4_0, rows, cols, w)
+    x = np.random.default_rng(3).standard_normal((200, cols)).astype(np.float32)
+    ctx.set_gemm_path(2)
+    try:
+        got = _run(ctx, torch, "blk.0.attn_output.weight", x, rows, noalloc=True)
+    finally:
+        ctx.set_gemm_path(0)
+    np.testing.assert_array_equal(got, oracle.qmatmul(synth.Q4_0, w, rows, cols, x, 200))
     dx = torch.zeros((17, cols), dtype=torch.float32, device="cuda")
     dy = torch.zeros((17, rows), dtype=torch.float32, device="cuda")
     ctx.set_gemm_path(4)
