@@ -74,6 +74,7 @@ def parse(argv=None):
     ap.add_argument("--shapes", default="", help="config 2: NxK list (default: the sweep's six)")
     ap.add_argument("--tokens", default="", help="config 2: M list (default 1,64,512,4096)")
     ap.add_argument("--gemm-path", type=int, default=0, help="shield_set_gemm_path for the run")
+    ap.add_argument("--attention-rows", type=int, default=0, help="shield_set_attention_rows for the run")
     ap.add_argument("--decode", default="", help="decode mode: comma list of sequence counts")
     ap.add_argument("--int8-peak", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="model configs: first N layers only (profiling a small case)")
@@ -386,6 +387,7 @@ def run_model(args) -> int:
     upload_s = time.perf_counter() - t_up
     upload_bytes = sum(int(t["data"].nbytes) for t in tensors.values())
     ctx.set_gemm_path(args.gemm_path)
+    ctx.set_attention_rows(args.attention_rows)
     vid = np.asarray(spec.verdict_ids, np.int32)
     nyes = len(spec.yes_ids)
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -509,7 +511,7 @@ def model_line(args, world, spec, tokens, reqs, fwd_ms, e2e_ms, per_rank, g, pea
                    "tokens_per_step": tokens // args.steps,
                    "parallelism": f"request shards x{world}, full weight replicas, no collective",
                    "l2": "inputs larger than L2 (the weights stream through every layer)",
-                   "gemm_path": args.gemm_path},
+                   "gemm_path": args.gemm_path, "attention_rows": args.attention_rows},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(per_rank[:, 5].sum()) // args.steps,
                 "d2h_bytes_per_step": int(per_rank[:, 6].sum()) // args.steps},
@@ -713,6 +715,7 @@ def run_decode(args) -> int:
         ctx.set_config(spec, max_positions=4096, max_batch_tokens=args.max_batch_tokens)
         ctx.upload_model(tensors)
         ctx.set_gemm_path(args.gemm_path)
+        ctx.set_attention_rows(args.attention_rows)
         stream = torch.cuda.ExternalStream(ctx.stream())
         rng = np.random.default_rng(SET_SEED)
         for b in _csv(args.decode, int):

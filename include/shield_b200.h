@@ -262,9 +262,9 @@ shield_status shield_debug_block_dots(shield_ctx *ctx, int32_t device, const cha
                                       int64_t M, int32_t *dots, int32_t path);
 
 /* Which GEMM kernel the context uses: 0 = automatic (1..16 tokens: one warp
- * per output row; otherwise tensor cores where the shape allows, long token
- * batches reading a once-unpacked f16 copy of the layer weights, short ones
- * unpacking the GGUF blocks on the fly), 1 = CUDA-core tiled kernel only,
+ * per output row; otherwise tensor cores where the shape allows, reading the
+ * once-unpacked f16 copy of a layer weight, or unpacking the GGUF blocks on
+ * the fly for a matrix without one), 1 = CUDA-core tiled kernel only,
  * 2 = tensor cores unpacking GGUF blocks only, 3 = tensor cores on the
  * unpacked copy only, 4 = the few-token kernels only. 2, 3 and 4 fail
  * with SHIELD_ERR_UNSUPPORTED on shapes their kernel does not take; the
@@ -277,6 +277,14 @@ shield_status shield_set_gemm_path(shield_ctx *ctx, int32_t path);
  * i.e. few tokens; else 128), 64 or 128 = that width only. Process-wide; the
  * outputs are identical at either width. For cross-checking. */
 shield_status shield_set_gemm_tile_width(shield_ctx *ctx, int32_t width);
+
+/* Query rows per CTA of the attention kernel: 0 = automatic (128, or 64
+ * when 128-row CTAs would be fewer than two per SM or less than half filled:
+ * few tokens, or one token per request), 64 or 128 = that size only (a
+ * multiple of the query heads per KV head, else later forwards fail with
+ * SHIELD_ERR_UNSUPPORTED). Per context; outputs are identical at either
+ * size. For cross-checking. */
+shield_status shield_set_attention_rows(shield_ctx *ctx, int32_t rows);
 
 /* Intermediate tensors of one layer, named as MinistralModel's
  * IActivationSink names them (MinistralModel.cs:212-237). */

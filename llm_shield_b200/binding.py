@@ -58,7 +58,7 @@ EXPORTS = [
     "shield_set_prefix_state", "shield_seq_create", "shield_seq_forward",
     "shield_seq_length", "shield_seq_reset", "shield_seq_release", "shield_qmatmul", "shield_qmatmul_device", "shield_qmatmul_noalloc",
     "shield_debug_block_dots",
-    "shield_set_gemm_path", "shield_set_gemm_tile_width", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
+    "shield_set_gemm_path", "shield_set_gemm_tile_width", "shield_set_attention_rows", "shield_debug_activation", "shield_set_timing", "shield_read_timing",
     "shield_device_stream", "shield_last_error",
 ]
 
@@ -97,6 +97,7 @@ def lib() -> C.CDLL:
         L.shield_debug_block_dots.argtypes = [P, C.c_int32, C.c_char_p, P, C.c_int64, P, C.c_int32]
         L.shield_set_gemm_path.argtypes = [P, C.c_int32]
         L.shield_set_gemm_tile_width.argtypes = [P, C.c_int32]
+        L.shield_set_attention_rows.argtypes = [P, C.c_int32]
         L.shield_debug_activation.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_int32, P]
         L.shield_device_stream.argtypes = [P, C.c_int32, C.POINTER(P)]
         L.shield_set_timing.argtypes = [P, C.c_int32]
@@ -303,6 +304,10 @@ class ShieldContext:
     def set_gemm_tile_width(self, width: int):
         """0: automatic; 64 or 128: the tensor-core GEMM's tile width only."""
         _check(lib().shield_set_gemm_tile_width(self._h, width))
+
+    def set_attention_rows(self, rows: int):
+        """0: automatic; 64 or 128 query rows per attention CTA only."""
+        _check(lib().shield_set_attention_rows(self._h, rows))
 
     def activation(self, ids, layer: int, what: int = ACT_OUTPUT, device: int = 0):
         """Tensor `what` (ACT_*) of layer `layer` for one request."""

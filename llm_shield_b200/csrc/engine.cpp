@@ -296,6 +296,7 @@ struct Ctx {
     Config cfg;
     bool configured = false;
     int gemm_path = 0;
+    int att_rows = 0;             // query rows per attention CTA: 0 = by the grid size
     std::vector<int32_t> prefix;  // token ids whose KV every device holds (empty: none)
     int64_t next_seq = 1;         // sequence ids: (device << 48) | serial
 };
@@ -381,6 +382,19 @@ static void gemm(Ctx &C, Device &d, const Tensor &W, const QAct &q, float *y, in
 // tensor-core launch covering all of them when the kernel takes them (the
 // tiles of every weight run side by side, which matters when few tokens make
 // few tiles), else one gemm() each. The outputs are identical either way.
+// Rows row_ids[0..n) of a weight for every token (the verdict head, row
+// subsets): the few-token kernels up to 16 tokens (every block's dot in
+// parallel, then each output's chain in block order), else the CUDA-core
+// tiled kernel; the same arithmetic either way. Path 1 keeps the tiled kernel.
+static cudaError_t launch_gemm_rows(const Ctx &C, const DevWeight &w, const int32_t *row_ids, int64_t n,
+                                    const QAct &q, float *y, int64_t ldy, cudaStream_t s) {
+    if (C.gemm_path != 1 && gemv_small_supports(w, q.M)) {
+        const cudaError_t e = launch_gemv_rows(w, row_ids, n, q, y, ldy, EPI_STORE, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    return launch_gemm_simt(w, row_ids, n, q, y, ldy, EPI_STORE, s);
+}
+
 static void gemm_shared_input(Ctx &C, Device &d, int count, const Tensor *const *W, const QAct &q, float *const *ys,
                               const int64_t *lds) {
     const DevWeight *ws[3];
@@ -546,18 +560,24 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
     }
     const int32_t *d_ids = b.meta, *d_pos = b.meta + M, *d_last = b.meta + 3 * M;
 
-    // attention: one work item per (request, 128/G query tokens), longest
+    // attention: one work item per (request, rows/G query tokens), longest
     // first (the CTAs of long rows start early instead of forming a tail), in
-    // groups whose scratch fits the buffer
-    // 64 query rows per CTA instead of 128 when 128-row items would give fewer
-    // than two CTAs per SM (small batches: a single short request)
+    // groups whose scratch fits the buffer. 128 query rows per CTA, or 64
+    // when 128-row items would give fewer than two CTAs per SM (a single
+    // short request) or be less than half filled (decode steps: one token per
+    // request). 32- and 16-row CTAs were slower in both cases (fewer threads
+    // to load each key tile; config 1 +2% / +7%, one-sequence decode +21%).
     const int G = c.n_heads / c.n_kv_heads;
-    int att_rows = attention_rows_per_cta();
-    {
-        int64_t n128 = 0;
-        for (int r = 0; r < R; r++) n128 += (B.len[r] + att_rows / G - 1) / (att_rows / G);
-        if (n128 * c.n_kv_heads < 2 * (int64_t)d.sms && (att_rows / 2) % G == 0) att_rows /= 2;
+    int att_rows = C.att_rows ? C.att_rows : attention_rows_per_cta();
+    if (!C.att_rows && (att_rows / 2) % G == 0) {
+        int64_t items = 0, rows_used = 0;
+        for (int r = 0; r < R; r++) {
+            items += (B.len[r] + att_rows / G - 1) / (att_rows / G);
+            rows_used += (int64_t)B.len[r] * G;
+        }
+        if (items * c.n_kv_heads < 2 * (int64_t)d.sms || 2 * rows_used < items * att_rows) att_rows /= 2;
     }
+    if (att_rows % G) throw Error(SHIELD_ERR_UNSUPPORTED, "attention rows per CTA must be a multiple of heads per KV head");
     const int QT = att_rows / G;
     struct AttGroup { int w0, nw; };
     struct AttItem { int64_t kend; int32_t r, q0; };
@@ -813,7 +833,7 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
         const Tensor &on = d.get("output_norm.weight");
         QAct qh = qact(b, R, c.hidden);
         count_launch(d), check_launch(launch_rmsnorm_quant(b.h, d_last, R, c.hidden, on.vec, c.eps, nullptr, qh, s), "final norm");
-        count_launch(d), check_launch(launch_gemm_simt(emb.w, b.verdict, nv, qh, b.logits, nv, EPI_STORE, s), "verdict head");
+        count_launch(d), check_launch(launch_gemm_rows(C, emb.w, b.verdict, nv, qh, b.logits, nv, s), "verdict head");
         if (f1 && f0) {
             cudaEventRecord(f1, s);
             T.fwd.emplace_back(f0, f1);
@@ -1517,7 +1537,7 @@ static void qmatmul_dev(Ctx &C, Device &d, const Tensor &W, const float *d_x, in
     QAct q = scratch_qact(d, M, W.w.cols);
     check_launch(launch_quantize(d_x, M, W.w.cols, W.w.cols, q, d.stream), "quantize");
     if (d_rows) {
-        check_launch(launch_gemm_simt(W.w, d_rows, n_rows, q, d_y, n_rows, EPI_STORE, d.stream), "row-subset GEMM");
+        check_launch(launch_gemm_rows(C, W.w, d_rows, n_rows, q, d_y, n_rows, d.stream), "row-subset GEMM");
     } else {
         if (!d.buf.err) {
             dev_alloc(d.buf.err, 1);
@@ -1804,6 +1824,14 @@ shield_status shield_set_gemm_tile_width(shield_ctx *ctx, int32_t width) {
         if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
         if (width != 0 && width != 64 && width != 128) throw Error(SHIELD_ERR_ARG, "width must be 0, 64 or 128");
         gemm_tc_set_tile_width(width);
+    });
+}
+
+shield_status shield_set_attention_rows(shield_ctx *ctx, int32_t rows) {
+    return guarded([&] {
+        if (!ctx) throw Error(SHIELD_ERR_ARG, "ctx is null");
+        if (rows != 0 && rows != 64 && rows != 128) throw Error(SHIELD_ERR_ARG, "rows must be 0, 64 or 128");
+        ctx->c.att_rows = rows;
     });
 }
 

@@ -463,7 +463,8 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
 }
 
 // RR query rows per CTA with 2 x RR threads: 128 for large batches, 64 for
-// small ones (twice the CTAs when few work items would leave SMs idle).
+// small or sparsely filled ones (twice the CTAs when few work items would
+// leave SMs idle; half the idle rows when items hold few tokens).
 template <int RR>
 __global__ void __launch_bounds__(2 * RR, RR == 128 ? 2 : 3) k_attn(const AttArgs A) {
     extern __shared__ float sm[];

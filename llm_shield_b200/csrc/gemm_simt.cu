@@ -274,8 +274,8 @@ __device__ __forceinline__ void words_to_i8x4(const uint32_t (&w)[BlockWords<TYP
 
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
-k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
-             const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds, int M,
+k_gemv_small(const uint8_t *__restrict__ W, const int32_t *__restrict__ row_ids, int64_t rows, int64_t row_bytes,
+             int64_t K, const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds, int M,
              float *__restrict__ y, int64_t ldy) {
     constexpr bool OFF = has_offset(TYPE);
     __shared__ int32_t s_dot[GEMV_WARPS][32][GEMV_MAX_TOKENS + 1];
@@ -285,7 +285,7 @@ k_gemv_small(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int
     const int64_t n = (int64_t)blockIdx.x * GEMV_WARPS + wid;
     if (n >= rows) return;  // whole warp
     const int64_t nb = K / 32;
-    const uint8_t *row = W + n * row_bytes;
+    const uint8_t *row = W + (row_ids ? (int64_t)row_ids[n] : n) * row_bytes;
     float f = 0.0f;  // lane m < M: token m's output
     for (int64_t c0 = 0; c0 < nb; c0 += 32) {
         const int64_t b = c0 + lane;
@@ -337,17 +337,20 @@ constexpr int GEMV1_ROWS = 16, GEMV1_THREADS = 256, GEMV1_CHUNK = 96, GEMV1_UNRO
 
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(GEMV1_THREADS)
-k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64_t K,
-           const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds,
+k_gemv_one(const uint8_t *__restrict__ W, const int32_t *__restrict__ row_ids, int64_t rows, int64_t row_bytes,
+           int64_t K, const int8_t *__restrict__ A, const float *__restrict__ da, const float *__restrict__ ds,
            float *__restrict__ y) {
     constexpr bool OFF = has_offset(TYPE);
     constexpr int LD = GEMV1_CHUNK + 1;  // odd row stride: phase 2's threads read distinct banks
     __shared__ int32_t s_dot[GEMV1_ROWS * LD];
     __shared__ float s_p[GEMV1_ROWS * LD];
     __shared__ float s_m[OFF ? GEMV1_ROWS * LD : 1];
+    __shared__ int64_t s_src[GEMV1_ROWS];  // weight row of each output row
     const int64_t n0 = (int64_t)blockIdx.x * GEMV1_ROWS;
     const int nrow = rows - n0 < GEMV1_ROWS ? (int)(rows - n0) : GEMV1_ROWS;
     const int64_t nb = K / 32;
+    if (threadIdx.x < nrow) s_src[threadIdx.x] = row_ids ? (int64_t)row_ids[n0 + threadIdx.x] : n0 + threadIdx.x;
+    __syncthreads();
     float f = 0.0f;  // thread r < nrow: row n0 + r
     for (int64_t c0 = 0; c0 < nb; c0 += GEMV1_CHUNK) {
         const int nc = nb - c0 < GEMV1_CHUNK ? (int)(nb - c0) : GEMV1_CHUNK;
@@ -360,7 +363,7 @@ k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64
                     const int r = i / nc, bl = i - r * nc;
                     const int64_t b = c0 + bl;
                     uint32_t bw[BlockWords<TYPE>::NW];
-                    load_block_words<TYPE>(W + (n0 + r) * row_bytes + b * block_bytes(TYPE), bw);
+                    load_block_words<TYPE>(W + s_src[r] * row_bytes + b * block_bytes(TYPE), bw);
                     int wq[8];
                     float dw, mw;
                     words_to_i8x4<TYPE>(bw, wq, dw, mw);
@@ -397,25 +400,28 @@ k_gemv_one(const uint8_t *__restrict__ W, int64_t rows, int64_t row_bytes, int64
     }
 }
 
+// n_out outputs per token: weight rows row_ids[0..n_out) (all rows in order
+// when row_ids is null).
 template <int TYPE>
-static void gemv_small_t(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s) {
+static void gemv_small_t(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                         int64_t ldy, int epi, cudaStream_t s) {
     if (q.M == 1) {
-        const unsigned g1 = (unsigned)((w.rows + GEMV1_ROWS - 1) / GEMV1_ROWS);
+        const unsigned g1 = (unsigned)((n_out + GEMV1_ROWS - 1) / GEMV1_ROWS);
         if (epi == EPI_ADD)
-            k_gemv_one<TYPE, EPI_ADD><<<g1, GEMV1_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.da,
-                                                                   q.ds, y);
+            k_gemv_one<TYPE, EPI_ADD><<<g1, GEMV1_THREADS, 0, s>>>(w.data, row_ids, n_out, w.row_bytes, w.cols, q.a8,
+                                                                   q.da, q.ds, y);
         else
-            k_gemv_one<TYPE, EPI_STORE><<<g1, GEMV1_THREADS, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8,
-                                                                     q.da, q.ds, y);
+            k_gemv_one<TYPE, EPI_STORE><<<g1, GEMV1_THREADS, 0, s>>>(w.data, row_ids, n_out, w.row_bytes, w.cols,
+                                                                     q.a8, q.da, q.ds, y);
         return;
     }
-    const unsigned grid = (unsigned)((w.rows + GEMV_WARPS - 1) / GEMV_WARPS);
+    const unsigned grid = (unsigned)((n_out + GEMV_WARPS - 1) / GEMV_WARPS);
     if (epi == EPI_ADD)
-        k_gemv_small<TYPE, EPI_ADD><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8, q.da,
-                                                                     q.ds, (int)q.M, y, ldy);
+        k_gemv_small<TYPE, EPI_ADD><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, row_ids, n_out, w.row_bytes, w.cols, q.a8,
+                                                                     q.da, q.ds, (int)q.M, y, ldy);
     else
-        k_gemv_small<TYPE, EPI_STORE><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, w.rows, w.row_bytes, w.cols, q.a8,
-                                                                       q.da, q.ds, (int)q.M, y, ldy);
+        k_gemv_small<TYPE, EPI_STORE><<<grid, GEMV_WARPS * 32, 0, s>>>(w.data, row_ids, n_out, w.row_bytes, w.cols,
+                                                                       q.a8, q.da, q.ds, (int)q.M, y, ldy);
 }
 
 bool gemv_small_supports(const DevWeight &w, int64_t M) {
@@ -423,14 +429,20 @@ bool gemv_small_supports(const DevWeight &w, int64_t M) {
 }
 
 cudaError_t launch_gemv_small(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s) {
+    return launch_gemv_rows(w, nullptr, w.rows, q, y, ldy, epi, s);
+}
+
+cudaError_t launch_gemv_rows(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                             int64_t ldy, int epi, cudaStream_t s) {
     if (!gemv_small_supports(w, q.M) || !q.a8 || reinterpret_cast<uintptr_t>(q.a8) % 16 || w.cols % 16)
         return cudaErrorNotSupported;
+    if (n_out == 0) return cudaSuccess;
     switch (w.type) {
-    case T_Q4_0: gemv_small_t<T_Q4_0>(w, q, y, ldy, epi, s); break;
-    case T_Q4_1: gemv_small_t<T_Q4_1>(w, q, y, ldy, epi, s); break;
-    case T_Q5_0: gemv_small_t<T_Q5_0>(w, q, y, ldy, epi, s); break;
-    case T_Q5_1: gemv_small_t<T_Q5_1>(w, q, y, ldy, epi, s); break;
-    case T_Q8_0: gemv_small_t<T_Q8_0>(w, q, y, ldy, epi, s); break;
+    case T_Q4_0: gemv_small_t<T_Q4_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q4_1: gemv_small_t<T_Q4_1>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q5_0: gemv_small_t<T_Q5_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q5_1: gemv_small_t<T_Q5_1>(w, row_ids, n_out, q, y, ldy, epi, s); break;
+    case T_Q8_0: gemv_small_t<T_Q8_0>(w, row_ids, n_out, q, y, ldy, epi, s); break;
     default: return cudaErrorNotSupported;
     }
     return cudaGetLastError();

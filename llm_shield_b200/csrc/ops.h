@@ -65,6 +65,9 @@ cudaError_t launch_unpack_f16(const DevWeight &w, cudaStream_t s);
 // row; the same arithmetic as the other GEMMs.
 bool gemv_small_supports(const DevWeight &w, int64_t M);
 cudaError_t launch_gemv_small(const DevWeight &w, const QAct &q, float *y, int64_t ldy, int epi, cudaStream_t s);
+// The same for weight rows row_ids[0..n_out) (the verdict head, row subsets).
+cudaError_t launch_gemv_rows(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
+                             int64_t ldy, int epi, cudaStream_t s);
 cudaError_t launch_gemm_simt(const DevWeight &w, const int32_t *row_ids, int64_t n_out, const QAct &q, float *y,
                              int64_t ldy, int epi, cudaStream_t s);
 // tcgen05 tensor-core GEMM; K % 256 == 0, full row range. Returns

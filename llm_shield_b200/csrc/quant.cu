@@ -239,12 +239,105 @@ __global__ void __launch_bounds__(256) k_rmsnorm_quant_rows(const float *__restr
     }
 }
 
+// The same RMSNorm + quantization for few rows (a single short request, the
+// final norm of the last positions), where 16 lanes per row leave most SMs
+// idle and each lane's 16-wide strided walk waits on one load per step. One
+// warp per row, two rows per CTA: the warp first stages its whole row in
+// shared memory with every load in flight, then lanes 0-15 (and, as copies,
+// 16-31) run the 16 chains from shared memory in the same order, and all 32
+// lanes normalize and quantize whole 32-blocks (blocks lane, lane + 32, ..).
+constexpr int RMS_WARP_ROWS = 2;
+
+__global__ void __launch_bounds__(32 * RMS_WARP_ROWS) k_rmsnorm_quant_warp(const float *__restrict__ x,
+                                                                            const int32_t *__restrict__ row_idx,
+                                                                            int64_t M, int K,
+                                                                            const float *__restrict__ w, float eps,
+                                                                            float *__restrict__ y, QAct q) {
+    extern __shared__ float4 s_rows[];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane & 15;
+    const int64_t t = (int64_t)blockIdx.x * RMS_WARP_ROWS + wid;
+    if (t >= M) return;  // whole warp; the warps of a CTA share no data
+    const int64_t src = row_idx ? row_idx[t] : t;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + src * (int64_t)K);
+    float4 *row4 = s_rows + (int64_t)wid * (K / 4);
+    const int n4 = K / 4;
+    {
+        int i = lane;
+        for (; i + 7 * 32 < n4; i += 8 * 32) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = __ldg(x4 + i + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 8; u++) row4[i + 32 * u] = v[u];
+        }
+        for (; i < n4; i += 32) row4[i] = __ldg(x4 + i);
+    }
+    __syncwarp();
+    const float *row = reinterpret_cast<const float *>(row4);
+    float acc = 0.0f;
+    for (int i = c; i < K; i += 16) acc = __fadd_rn(acc, __fmul_rn(row[i], row[i]));
+    // Vector.Sum of partials 0-7 and 8-15, then the two halves in double
+    float v = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
+    const float hi = __shfl_down_sync(0xffffffffu, v, 8);
+    float scale = 0.0f;
+    if (lane == 0) {
+        const double sum = __dadd_rn((double)v, (double)hi);
+        const float ms = __double2float_rn(__ddiv_rn(sum, (double)K));
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    }
+    scale = __shfl_sync(0xffffffffu, scale, 0);
+    const int nb = K / 32;
+    for (int b = lane; b < nb; b += 32) {
+        float vals[32];
+        const float4 *xs = row4 + b * 8;
+        const float4 *ws = reinterpret_cast<const float4 *>(w + b * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 xv = xs[i], wv = __ldg(ws + i);
+            vals[4 * i + 0] = __fmul_rn(__fmul_rn(xv.x, scale), wv.x);
+            vals[4 * i + 1] = __fmul_rn(__fmul_rn(xv.y, scale), wv.y);
+            vals[4 * i + 2] = __fmul_rn(__fmul_rn(xv.z, scale), wv.z);
+            vals[4 * i + 3] = __fmul_rn(__fmul_rn(xv.w, scale), wv.w);
+        }
+        if (y) {
+            float4 *ys = reinterpret_cast<float4 *>(y + t * (int64_t)K + b * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++) ys[i] = make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);
+        }
+        store_quantized_block(vals, t, b, K, q);
+    }
+}
+
+static int device_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+    }
+    return n;
+}
+
 cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
                                  float eps, float *y, const QAct &q, cudaStream_t s) {
     if (M == 0) return cudaSuccess;
     if (K % 32 == 0 && aligned16(x) && aligned16(w) && aligned16(y) && aligned16(q.a8) && aligned16(q.a16)) {
         const int64_t threads = M * 16;
-        k_rmsnorm_quant_rows<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, row_idx, M, K, w, eps, y, q);
+        const size_t smem = (size_t)RMS_WARP_ROWS * K * 4;
+        if ((threads + 255) / 256 < 2 * device_sms() && smem <= 200 * 1024) {
+            // fewer than two waves of the 16-lane kernel
+            if (smem > 48 * 1024) {
+                const cudaError_t e =
+                    cudaFuncSetAttribute(k_rmsnorm_quant_warp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                if (e != cudaSuccess) return e;
+            }
+            k_rmsnorm_quant_warp<<<(unsigned)((M + RMS_WARP_ROWS - 1) / RMS_WARP_ROWS), 32 * RMS_WARP_ROWS, smem, s>>>(
+                x, row_idx, M, K, w, eps, y, q);
+        } else {
+            k_rmsnorm_quant_rows<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, row_idx, M, K, w, eps, y, q);
+        }
     } else {
         k_rmsnorm_quant<<<(unsigned)M, 128, 0, s>>>(x, row_idx, K, w, eps, y, q);
     }

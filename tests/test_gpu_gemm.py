@@ -119,15 +119,25 @@ def test_token_result_does_not_depend_on_batch(ctx, qtype):
 
 @pytest.mark.parametrize("qtype", INT_TYPES)
 def test_row_subset_bit_identical(ctx, qtype):
-    """MatMulTilingTests.cs:67-95: out of order, repeated, across group boundaries."""
-    rows, cols, tokens = 100, 256, 5
-    ids = [99, 0, 57, 57, 8, 7, 64, 63, 98]
+    """MatMulTilingTests.cs:67-95: out of order, repeated, across group
+    boundaries; 1 and 2..16 tokens on the few-token kernels (one token: 16
+    output rows per CTA, so 20 ids end in a partial CTA), 40 tokens on the
+    tiled CUDA-core kernel, and the tiled kernel alone (path 1)."""
+    rows, cols = 100, 256
+    ids = [99, 0, 57, 57, 8, 7, 64, 63, 98, 1, 2, 3, 4, 5, 6, 9, 10, 11, 12, 99]
     w = random_weights(qtype, rows, cols, seed=5)
-    x = np.random.default_rng(6).uniform(-1, 1, (tokens, cols)).astype(np.float32)
     upload(ctx, "blk.0.attn_output.weight", qtype, rows, cols, w)
-    full = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows)
-    sub = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows, row_ids=ids)
-    np.testing.assert_array_equal(sub, full[:, ids])
+    for tokens in (1, 5, 16, 40):
+        x = np.random.default_rng(6 + tokens).uniform(-1, 1, (tokens, cols)).astype(np.float32)
+        full = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows)
+        np.testing.assert_array_equal(full, oracle.qmatmul(qtype, w, rows, cols, x, tokens), err_msg=f"{tokens}")
+        for path in (0, 1):
+            ctx.set_gemm_path(path)
+            try:
+                sub = ctx.qmatmul("blk.0.attn_output.weight", x, tokens, rows, row_ids=ids)
+            finally:
+                ctx.set_gemm_path(0)
+            np.testing.assert_array_equal(sub, full[:, ids], err_msg=f"{tokens} tokens, path {path}")
 
 
 def test_row_subset_rejects_ids_outside_the_matrix(ctx):

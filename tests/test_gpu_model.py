@@ -57,6 +57,23 @@ def test_ragged_batch_matches_oracle(small):
     check_against_oracle(om, spec, reqs, yes, no, score, logits)
 
 
+@pytest.mark.parametrize("rows", [64, 128])
+def test_attention_rows_per_cta_bit_identical_to_oracle(small, rows):
+    """Both sizes of the attention kernel's CTA (64 or 128 query rows; the
+    automatic choice takes 64 for small or sparsely filled micro-batches)
+    give the oracle's logits bit for bit, with requests that end inside and
+    exactly at a CTA's rows."""
+    spec, _, ctx, om = small
+    lengths = [1, 4, 5, 17, 64, 130]
+    reqs = synth.random_requests(len(lengths), lengths, seed=rows, vocab=spec.vocab)
+    ctx.set_attention_rows(rows)
+    try:
+        yes, no, score, logits = ctx.score_batch(reqs, spec.verdict_ids, len(spec.yes_ids))
+    finally:
+        ctx.set_attention_rows(0)
+    check_against_oracle(om, spec, reqs, yes, no, score, logits)
+
+
 def test_results_do_not_depend_on_batching(small):
     """A request's logits are bit-identical alone and inside any batch."""
     spec, _, ctx, _ = small
