@@ -241,57 +241,66 @@ __global__ void __launch_bounds__(256) k_rmsnorm_quant_rows(const float *__restr
 
 // The same RMSNorm + quantization for few rows (a single short request, the
 // final norm of the last positions), where 16 lanes per row leave most SMs
-// idle and each lane's 16-wide strided walk waits on one load per step. One
-// warp per row, two rows per CTA: the warp first stages its whole row in
-// shared memory with every load in flight, then lanes 0-15 (and, as copies,
-// 16-31) run the 16 chains from shared memory in the same order, and all 32
-// lanes normalize and quantize whole 32-blocks (blocks lane, lane + 32, ..).
-constexpr int RMS_WARP_ROWS = 2;
+// idle and each lane's strided walk waits on one load per step. One CTA of
+// 128 threads per row: the row is staged in shared memory with every load in
+// flight; lanes 0-15 of warp 0 (16-31 as copies) run the 16 chains from
+// shared memory in the same order, eight squares formed ahead of their adds;
+// then every thread normalizes and quantizes whole 32-blocks (block tid,
+// tid + 128, ..).
+constexpr int RMS_CTA_THREADS = 128;
 
-__global__ void __launch_bounds__(32 * RMS_WARP_ROWS) k_rmsnorm_quant_warp(const float *__restrict__ x,
-                                                                            const int32_t *__restrict__ row_idx,
-                                                                            int64_t M, int K,
-                                                                            const float *__restrict__ w, float eps,
-                                                                            float *__restrict__ y, QAct q) {
-    extern __shared__ float4 s_rows[];
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane & 15;
-    const int64_t t = (int64_t)blockIdx.x * RMS_WARP_ROWS + wid;
-    if (t >= M) return;  // whole warp; the warps of a CTA share no data
+__global__ void __launch_bounds__(RMS_CTA_THREADS) k_rmsnorm_quant_cta(const float *__restrict__ x,
+                                                                       const int32_t *__restrict__ row_idx, int K,
+                                                                       const float *__restrict__ w, float eps,
+                                                                       float *__restrict__ y, QAct q) {
+    extern __shared__ float4 s_row4[];
+    __shared__ float s_scale;
+    const int tid = threadIdx.x, lane = tid & 31, c = lane & 15;
+    const int64_t t = blockIdx.x;
     const int64_t src = row_idx ? row_idx[t] : t;
     const float4 *x4 = reinterpret_cast<const float4 *>(x + src * (int64_t)K);
-    float4 *row4 = s_rows + (int64_t)wid * (K / 4);
     const int n4 = K / 4;
     {
-        int i = lane;
-        for (; i + 7 * 32 < n4; i += 8 * 32) {
-            float4 v[8];
+        int i = tid;
+        for (; i + 5 * RMS_CTA_THREADS < n4; i += 6 * RMS_CTA_THREADS) {
+            float4 v[6];
 #pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = __ldg(x4 + i + 32 * u);
+            for (int u = 0; u < 6; u++) v[u] = __ldg(x4 + i + RMS_CTA_THREADS * u);
 #pragma unroll
-            for (int u = 0; u < 8; u++) row4[i + 32 * u] = v[u];
+            for (int u = 0; u < 6; u++) s_row4[i + RMS_CTA_THREADS * u] = v[u];
         }
-        for (; i < n4; i += 32) row4[i] = __ldg(x4 + i);
+        for (; i < n4; i += RMS_CTA_THREADS) s_row4[i] = __ldg(x4 + i);
     }
-    __syncwarp();
-    const float *row = reinterpret_cast<const float *>(row4);
-    float acc = 0.0f;
-    for (int i = c; i < K; i += 16) acc = __fadd_rn(acc, __fmul_rn(row[i], row[i]));
-    // Vector.Sum of partials 0-7 and 8-15, then the two halves in double
-    float v = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
-    const float hi = __shfl_down_sync(0xffffffffu, v, 8);
-    float scale = 0.0f;
-    if (lane == 0) {
-        const double sum = __dadd_rn((double)v, (double)hi);
-        const float ms = __double2float_rn(__ddiv_rn(sum, (double)K));
-        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    __syncthreads();
+    const float *row = reinterpret_cast<const float *>(s_row4);
+    if (tid < 32) {
+        float acc = 0.0f;
+        int i = c;
+        for (; i + 7 * 16 < K; i += 8 * 16) {
+            float sq[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) sq[u] = __fmul_rn(row[i + 16 * u], row[i + 16 * u]);
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, sq[u]);
+        }
+        for (; i < K; i += 16) acc = __fadd_rn(acc, __fmul_rn(row[i], row[i]));
+        // Vector.Sum of partials 0-7 and 8-15, then the two halves in double
+        float v = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+        v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
+        v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
+        const float hi = __shfl_down_sync(0xffffffffu, v, 8);
+        if (lane == 0) {
+            const double sum = __dadd_rn((double)v, (double)hi);
+            const float ms = __double2float_rn(__ddiv_rn(sum, (double)K));
+            s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+        }
     }
-    scale = __shfl_sync(0xffffffffu, scale, 0);
+    __syncthreads();
+    const float scale = s_scale;
     const int nb = K / 32;
-    for (int b = lane; b < nb; b += 32) {
+    for (int b = tid; b < nb; b += RMS_CTA_THREADS) {
         float vals[32];
-        const float4 *xs = row4 + b * 8;
+        const float4 *xs = s_row4 + b * 8;
         const float4 *ws = reinterpret_cast<const float4 *>(w + b * 32);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -325,16 +334,15 @@ cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t
     if (M == 0) return cudaSuccess;
     if (K % 32 == 0 && aligned16(x) && aligned16(w) && aligned16(y) && aligned16(q.a8) && aligned16(q.a16)) {
         const int64_t threads = M * 16;
-        const size_t smem = (size_t)RMS_WARP_ROWS * K * 4;
-        if ((threads + 255) / 256 < 2 * device_sms() && smem <= 200 * 1024) {
+        const size_t smem = (size_t)K * 4;
+        if ((threads + 255) / 256 < 2 * device_sms() && smem <= 200 * 1024 && M <= 0x7fffffff) {
             // fewer than two waves of the 16-lane kernel
             if (smem > 48 * 1024) {
                 const cudaError_t e =
-                    cudaFuncSetAttribute(k_rmsnorm_quant_warp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                    cudaFuncSetAttribute(k_rmsnorm_quant_cta, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
                 if (e != cudaSuccess) return e;
             }
-            k_rmsnorm_quant_warp<<<(unsigned)((M + RMS_WARP_ROWS - 1) / RMS_WARP_ROWS), 32 * RMS_WARP_ROWS, smem, s>>>(
-                x, row_idx, M, K, w, eps, y, q);
+            k_rmsnorm_quant_cta<<<(unsigned)M, RMS_CTA_THREADS, smem, s>>>(x, row_idx, K, w, eps, y, q);
         } else {
             k_rmsnorm_quant_rows<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, row_idx, M, K, w, eps, y, q);
         }
