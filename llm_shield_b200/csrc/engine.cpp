@@ -738,10 +738,11 @@ static void forward_batch(Ctx &C, Device &d, const int32_t *ids_host, const Batc
             const int64_t lds[3] = {c.qdim(), c.kvdim(), c.kvdim()};
             gemm_shared_input(C, d, 3, W, qa, ys, lds);
         }
-        count_launch(d), check_launch(launch_rope(b.q, M, c.n_heads, c.head_dim, c.qdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 d.temp, b.ctx, s, l == capture_layer && capture_what == SHIELD_ACT_Q_ROPE), "rope q");
-        count_launch(d), check_launch(launch_rope(b.k, M, c.n_kv_heads, c.head_dim, c.kvdim(), d_pos, d.cos_t, d.sin_t, c.rope_half,
-                                 nullptr, b.kc, s, l == capture_layer && capture_what == SHIELD_ACT_K_ROPE), "rope k");
+        count_launch(d), check_launch(launch_rope_qk(b.q, c.n_heads, b.k, c.n_kv_heads, M, c.head_dim, d_pos, d.cos_t,
+                                                    d.sin_t, c.rope_half, d.temp, b.ctx, b.kc,
+                                                    l == capture_layer && capture_what == SHIELD_ACT_Q_ROPE,
+                                                    l == capture_layer && capture_what == SHIELD_ACT_K_ROPE, s),
+                                     "rope");
         cap(l, SHIELD_ACT_Q_ROPE, b.q, c.qdim());
         cap(l, SHIELD_ACT_K_ROPE, b.k, c.kvdim());
         cap(l, SHIELD_ACT_V, b.v, c.kvdim());

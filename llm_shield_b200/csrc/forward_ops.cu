@@ -18,6 +18,7 @@ constexpr int PKT = 32;      // keys per PV tile
 constexpr int LDP = PKT + 4; // padded row of a PV weight tile
 }  // namespace att
 
+
 // Scratch row stride of a CTA whose rows attend to kend keys: a multiple of 4
 // floats, so every row starts on a 16-byte boundary.
 __device__ __forceinline__ int64_t att_ld(int64_t kend) { return (kend + 3) & ~int64_t(3); }
@@ -75,16 +76,31 @@ __global__ void k_rope(float *__restrict__ x, int64_t M, int heads, int head_dim
 // row of 128 dims, lane l taking dims 4l..4l+3 (pairs 2l, 2l+1; pairs from
 // `half` on are not rotated, as in Rope.Apply). The rotated row goes to perm
 // in chain-major order through a shared-memory transpose (16-byte stores),
-// and back to x in place only when natural is set.
-__global__ void __launch_bounds__(256) k_rope_rows(float *__restrict__ x, int64_t rows, int heads, int64_t ld,
+// and back to x in place only when natural is set. One launch covers two
+// tensors (the queries, then the keys): rows below rows0 belong to set 0.
+struct RopeSet {
+    float *x, *perm;
+    const float *temp;  // attention temperature per position, or null
+    int64_t ld;
+    int heads;
+    bool natural;
+};
+
+__global__ void __launch_bounds__(256) k_rope_rows(const RopeSet s0, const RopeSet s1, int64_t rows0, int64_t rows,
                                                    const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
-                                                   const float *__restrict__ sin_t, int half,
-                                                   const float *__restrict__ temp, float *__restrict__ perm,
-                                                   bool natural) {
+                                                   const float *__restrict__ sin_t, int half) {
     __shared__ float srow[8][att::HD];
     const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * 8 + wid;
+    int64_t row = (int64_t)blockIdx.x * 8 + wid;
     if (row >= rows) return;  // whole warp
+    const bool first = row < rows0;  // warp-uniform
+    if (!first) row -= rows0;
+    float *const x = first ? s0.x : s1.x;
+    float *const perm = first ? s0.perm : s1.perm;
+    const float *const temp = first ? s0.temp : s1.temp;
+    const int64_t ld = first ? s0.ld : s1.ld;
+    const int heads = first ? s0.heads : s1.heads;
+    const bool natural = first ? s0.natural : s1.natural;
     const int64_t t = row / heads;
     const int h = (int)(row % heads);
     const int ps = pos[t];
@@ -115,16 +131,20 @@ __global__ void __launch_bounds__(256) k_rope_rows(float *__restrict__ x, int64_
         *reinterpret_cast<const float4 *>(&srow[wid][4 * lane]);
 }
 
+static bool rope_rows_ok(const float *x, int head_dim, int64_t ld, const float *perm) {
+    return head_dim == att::HD && ld % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(perm) % 16 == 0;
+}
+
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
                         cudaStream_t s, bool natural) {
     if (M == 0) return cudaSuccess;
     if (perm) {
-        if (head_dim != att::HD || ld % 4 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(perm) % 16)
-            return cudaErrorInvalidValue;
+        if (!rope_rows_ok(x, head_dim, ld, perm)) return cudaErrorInvalidValue;
         const int64_t rows = M * heads;
-        k_rope_rows<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, rows, heads, ld, pos, cos_t, sin_t, half, temp, perm,
-                                                               natural);
+        const RopeSet rs{x, perm, temp, ld, heads, natural};
+        k_rope_rows<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(rs, rs, rows, rows, pos, cos_t, sin_t, half);
         return cudaGetLastError();
     }
     int64_t n = M * heads * half;
@@ -134,11 +154,25 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
     return cudaGetLastError();
 }
 
+cudaError_t launch_rope_qk(float *q, int q_heads, float *k, int k_heads, int64_t M, int head_dim, const int32_t *pos,
+                           const float *cos_t, const float *sin_t, int half, const float *q_temp, float *q_perm,
+                           float *k_perm, bool q_natural, bool k_natural, cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    const int64_t q_ld = (int64_t)q_heads * head_dim, k_ld = (int64_t)k_heads * head_dim;
+    if (!rope_rows_ok(q, head_dim, q_ld, q_perm) || !rope_rows_ok(k, head_dim, k_ld, k_perm))
+        return cudaErrorInvalidValue;
+    const RopeSet qs{q, q_perm, q_temp, q_ld, q_heads, q_natural}, ks{k, k_perm, nullptr, k_ld, k_heads, k_natural};
+    const int64_t rows0 = M * q_heads, rows = rows0 + M * k_heads;
+    k_rope_rows<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(qs, ks, rows0, rows, pos, cos_t, sin_t, half);
+    return cudaGetLastError();
+}
+
 // Causal grouped-query attention over a ragged batch (AttendGroup,
 // MinistralModel.cs:372-440) in one kernel that keeps the oracle's exact
 // operation order, so the context is bit-identical to it. One CTA owns 128
-// query rows (64 for small batches, which then get twice the CTAs) of one
-// request and one KV head: 128/G tokens x the G query heads
+// query rows (64 for small batches, which then get twice the CTAs, each with
+// as many threads as a 128-row one) of one request and one KV head: rows/G
+// tokens x the G query heads
 // sharing that KV head, so each key and value row is read once per CTA for all
 // of them. A request's queries are its tokens in the batch; its keys are the
 // first pre positions of its cache (the system-prompt cache of
@@ -150,12 +184,11 @@ cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld
 //            = fma over dims j, j+8, .., j+120 in order (Kernels.Dot4); every
 //            score goes to the CTA's scratch rows and its row maximum is kept
 //   phase 2  per row: e = shield_expf(s - max) in place, summed as 32
-//            lane-strided partials folded pairwise (Kernels.Softmax)
-//   phase 3  ctx[d] = fma(v[p][d], e[p] / sum, ctx[d]) over p in order
-//            (AddScaled4), the division done once per weight as its tile
-//            arrives in shared memory
+//            lane-strided partials folded pairwise (Kernels.Softmax), then
+//            w = e / sum in place
+//   phase 3  ctx[d] = fma(v[p][d], w[p], ctx[d]) over p in order (AddScaled4)
 //
-// The scratch rows of a CTA (128 x round_up(kend, 4) floats) are written and
+// The scratch rows of a CTA (rows x round_up(kend, 4) floats) are written and
 // read back within its lifetime, so short requests' scores never leave L2.
 // Work items arrive longest first (host side), so the long CTAs of a ragged
 // batch start early instead of forming a tail.
@@ -166,6 +199,21 @@ struct AttView {
     int64_t start, ld;             // first batch row, scratch row stride
     float *sc;                     // this CTA's 128 scratch rows
     const float *ck, *cv;          // this layer's cached keys and values (pre > 0)
+};
+
+// Thread layout of a CTA: RR query rows, TPR threads per row. TPR = 2 (RR/16
+// warps): a phase-1 key tile is 32 keys, a phase-3 thread owns 4 rows.
+// TPR = 4 (twice the warps for the same rows, for small batches where one
+// CTA per SM is all there is): the phase-1 tile is 64 keys, warps w and
+// w + RR/16 taking its two 32-key halves, and a phase-3 thread owns 2 rows.
+template <int RR, int TPR>
+struct AttShape {
+    static constexpr int THREADS = TPR * RR;
+    static constexpr int KH = TPR / 2;           // key halves of a phase-1 tile
+    static constexpr int KTE = att::KT * KH;     // keys of a phase-1 tile
+    static constexpr int NA = 8 * RR / THREADS;  // rows per phase-3 thread
+    static constexpr int RSTEP = THREADS / 8;    // phase-3 row stride
+    static_assert(TPR == 2 || TPR == 4, "2 or 4 threads per row");
 };
 
 template <int RR>
@@ -196,15 +244,17 @@ __device__ __forceinline__ const float *kv_row(const float *own, const float *ca
     return p < w.pre ? cached + (int64_t)p * kvdim : own + (w.start + p - w.pre) * kvdim;
 }
 
-// Phase 1: the CTA's 128 x kend scores into its scratch rows, and each row's
-// maximum into rowmax[] (shared). Keys and the CTA's query rows arrive in
-// chain-major order (see chain_pos) by cp.async, key tiles double-buffered.
-// Thread (warp, rl, kl) owns rows warp*16 + rl + 4a and keys kl + 8b of a tile.
-template <int RR>
+// Phase 1: the CTA's RR x kend scores into its scratch rows, and each row's
+// maximum over each key half into rowmax[half][row] (shared). Keys and the
+// CTA's query rows arrive in chain-major order (see chain_pos) by cp.async,
+// key tiles double-buffered. Thread (warp = wr + (RR/16) kh, rl, kl) owns rows
+// wr*16 + rl + 4a and keys 32 kh + kl + 8b of a tile.
+template <int RR, int TPR>
 __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, float *sm, float *rowmax) {
     using namespace att;
-    constexpr int R = RR, THREADS = 2 * RR;  // rows of the CTA, its threads
-    float *Qs = sm;  // R x LD, then two KT x LD key tiles
+    using S = AttShape<RR, TPR>;
+    constexpr int R = RR, THREADS = S::THREADS, KTE = S::KTE;
+    float *Qs = sm;  // R x LD, then two KTE x LD key tiles
     const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
     const int64_t qdim = (int64_t)A.n_heads * HD, kvdim = (int64_t)A.n_kv_heads * HD;
@@ -212,10 +262,10 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
     const uint32_t kbase = (uint32_t)__cvta_generic_to_shared(sm + R * LD);
     auto load = [&](int st, int kt0) {
 #pragma unroll
-        for (int it = 0; it < KT * (HD / 4) / THREADS; it++) {
+        for (int it = 0; it < KTE * (HD / 4) / THREADS; it++) {
             const int idx = tid + it * THREADS, kk = idx / (HD / 4), c4 = idx % (HD / 4), p = kt0 + kk;
             const bool ok = p < w.kend;
-            cp_async16(kbase + (uint32_t)(st * KT * LD + kk * LD + c4 * 4) * 4,
+            cp_async16(kbase + (uint32_t)(st * KTE * LD + kk * LD + c4 * 4) * 4,
                        ok ? kv_row(A.kc, w.ck, w, p, kvdim) + (int64_t)h * HD + c4 * 4 : A.kc, ok);
         }
     };
@@ -231,21 +281,22 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
     load(0, 0);
     cp_async_commit();
     const int warp = tid >> 5, lane = tid & 31;
+    const int wr = warp % (R / 16), kh = warp / (R / 16);  // row group, key half
     const int rl = lane >> 3, kl = lane & 7;
     int limit[4];  // keys each of the thread's rows attends to
     float mx[4];
 #pragma unroll
     for (int a = 0; a < 4; a++) {
-        const int row = warp * 16 + rl + 4 * a, tok = w.q0 + row / G;
+        const int row = wr * 16 + rl + 4 * a, tok = w.q0 + row / G;
         limit[a] = tok < w.len ? w.pre + tok + 1 : 0;
         mx[a] = -INFINITY;
     }
-    for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += KT, st ^= 1) {
-        if (kt0 + KT < w.kend) load(st ^ 1, kt0 + KT);
+    for (int kt0 = 0, st = 0; kt0 < w.kend; kt0 += KTE, st ^= 1) {
+        if (kt0 + KTE < w.kend) load(st ^ 1, kt0 + KTE);
         cp_async_commit();
         cp_async_wait1();
         __syncthreads();
-        const float *Ks = sm + R * LD + st * KT * LD;
+        const float *Ks = sm + R * LD + (st * KTE + kh * KT) * LD;
         // chains j and j+4 of each of the 4 x 4 (row, key) scores as one f32
         // pair: each lane of a packed fma is the scalar fma of its chain
         float T[16], U[16];
@@ -257,7 +308,7 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
                 float4 qa[4], kb[4];
 #pragma unroll
                 for (int a = 0; a < 4; a++)
-                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(warp * 16 + rl + 4 * a) * LD + j * 32 + s]);
+                    qa[a] = *reinterpret_cast<const float4 *>(&Qs[(wr * 16 + rl + 4 * a) * LD + j * 32 + s]);
 #pragma unroll
                 for (int b = 0; b < 4; b++)
                     kb[b] = *reinterpret_cast<const float4 *>(&Ks[(kl + 8 * b) * LD + j * 32 + s]);
@@ -287,10 +338,10 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
         for (int o = 0; o < 16; o++) U[o] = __fadd_rn(U[o], __fadd_rn(lo_f(c2[o]), hi_f(c2[o])));
 #pragma unroll
         for (int a = 0; a < 4; a++) {
-            float *dst = w.sc + (int64_t)(warp * 16 + rl + 4 * a) * w.ld;
+            float *dst = w.sc + (int64_t)(wr * 16 + rl + 4 * a) * w.ld;
 #pragma unroll
             for (int b = 0; b < 4; b++) {
-                const int p = kt0 + kl + 8 * b;
+                const int p = kt0 + kh * KT + kl + 8 * b;
                 if (p < limit[a]) {
                     const float s = __fmul_rn(__fadd_rn(T[a * 4 + b], U[a * 4 + b]), A.scale);
                     dst[p] = s;
@@ -307,24 +358,26 @@ __device__ __forceinline__ void attn_scores(const AttArgs &A, const AttView &w, 
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        if (kl == 0) rowmax[warp * 16 + rl + 4 * a] = m;
+        if (kl == 0) rowmax[kh * R + wr * 16 + rl + 4 * a] = m;
     }
 }
 
 // Phase 2: one warp per row, rows warp, warp + 8, ..: e = exp(s - max) in
 // place summed as 32 lane-strided partials, then w = e / sum in place; a row
 // whose maximum is not finite becomes uniform (Kernels.Softmax).
-template <int RR>
+template <int RR, int TPR>
 __device__ __forceinline__ void attn_softmax(const AttArgs &A, const AttView &w, const float *rowmax) {
     using namespace att;
-    constexpr int R = RR, THREADS = 2 * RR;
+    using S = AttShape<RR, TPR>;
+    constexpr int R = RR, THREADS = S::THREADS;
     const int G = A.n_heads / A.n_kv_heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int row = warp; row < R; row += THREADS / 32) {
         const int tok = w.q0 + row / G;
         if (tok >= w.len) continue;
         const int limit = w.pre + tok + 1;
-        const float mx = rowmax[row];
+        // the maximum is exact in any order: over the key halves, then the two
+        const float mx = S::KH == 1 ? rowmax[row] : fmaxf(rowmax[row], rowmax[R + row]);
         float *s = w.sc + (int64_t)row * w.ld;
         // phase 3 loads weights in 4-key granules: the keys after the row's own
         // position in its last granule must read as 0
@@ -369,13 +422,14 @@ __device__ __forceinline__ void attn_softmax(const AttArgs &A, const AttView &w,
 
 // Phase 3: ctx[row][d] = sum over keys p in order of fma(v[p][d], w[row][p], .)
 // with w = e / sum (MinistralModel.cs:372-440). Key tiles of V and of the
-// exp values are double-buffered in shared memory by cp.async; each weight
-// tile is divided once in place (masked keys to 0) before use. Thread (tr, td)
-// owns rows tr + 32a and dims td*4 + 32e (a, e < 4).
-template <int RR>
+// weights (masked keys read as 0) are double-buffered in shared memory by
+// cp.async. Thread (tr, td) owns rows tr + RSTEP*a (a < NA) and dims
+// td*4 + 32e (e < 4).
+template <int RR, int TPR>
 __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, float *sm) {
     using namespace att;
-    constexpr int R = RR, THREADS = 2 * RR, RSTEP = THREADS / 8;  // thread (tr, td) owns rows tr + RSTEP*a
+    using S = AttShape<RR, TPR>;
+    constexpr int R = RR, THREADS = S::THREADS, RSTEP = S::RSTEP, NA = S::NA;
     constexpr int V_FLOATS = PKT * LD, W_FLOATS = R * LDP;
     const int G = A.n_heads / A.n_kv_heads;
     const int h = blockIdx.y;
@@ -400,23 +454,23 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
             cp_async16(wb + (uint32_t)(row * LDP + c4 * 4) * 4, ok ? w.sc + (int64_t)row * w.ld + p : w.sc, ok);
         }
     };
-    // c2[a][2e + h]: dims td*4 + 32e + 2h + {0, 1} of row tr + 32a, as f32 pairs;
-    // each lane of a packed fma is the scalar fma(v[d], w, c[d])
-    uint64_t c2[4][8];
+    // c2[a][2e + h]: dims td*4 + 32e + 2h + {0, 1} of row tr + RSTEP*a, as f32
+    // pairs; each lane of a packed fma is the scalar fma(v[d], w, c[d])
+    uint64_t c2[NA][8];
 #pragma unroll
-    for (int a = 0; a < 4; a++)
+    for (int a = 0; a < NA; a++)
 #pragma unroll
         for (int e = 0; e < 8; e++) c2[a][e] = 0;
-    auto key = [&](uint32_t vrow, const float (&wa)[4]) {
-        uint64_t wd[4];
+    auto key = [&](uint32_t vrow, const float (&wa)[NA]) {
+        uint64_t wd[NA];
 #pragma unroll
-        for (int a = 0; a < 4; a++) wd[a] = pack2u(__float_as_uint(wa[a]), __float_as_uint(wa[a]));
+        for (int a = 0; a < NA; a++) wd[a] = pack2u(__float_as_uint(wa[a]), __float_as_uint(wa[a]));
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             uint64_t v0, v1;
             asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "r"(vrow + (td * 4 + 32 * e) * 4));
 #pragma unroll
-            for (int a = 0; a < 4; a++) {
+            for (int a = 0; a < NA; a++) {
                 c2[a][2 * e] = fma2(v0, wd[a], c2[a][2 * e]);
                 c2[a][2 * e + 1] = fma2(v1, wd[a], c2[a][2 * e + 1]);
             }
@@ -434,24 +488,27 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
         const int kn = min(PKT, w.kend - kt0);
         int kk = 0;
         for (; kk + 4 <= kn; kk += 4) {
-            float4 wt[4];
+            float4 wt[NA];
 #pragma unroll
-            for (int a = 0; a < 4; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + RSTEP * a) * LDP + kk]);
-            key(vs + (uint32_t)((kk + 0) * LD) * 4, {wt[0].x, wt[1].x, wt[2].x, wt[3].x});
-            key(vs + (uint32_t)((kk + 1) * LD) * 4, {wt[0].y, wt[1].y, wt[2].y, wt[3].y});
-            key(vs + (uint32_t)((kk + 2) * LD) * 4, {wt[0].z, wt[1].z, wt[2].z, wt[3].z});
-            key(vs + (uint32_t)((kk + 3) * LD) * 4, {wt[0].w, wt[1].w, wt[2].w, wt[3].w});
+            for (int a = 0; a < NA; a++) wt[a] = *reinterpret_cast<const float4 *>(&W[(tr + RSTEP * a) * LDP + kk]);
+            float wx[NA], wy[NA], wz[NA], ww[NA];
+#pragma unroll
+            for (int a = 0; a < NA; a++) wx[a] = wt[a].x, wy[a] = wt[a].y, wz[a] = wt[a].z, ww[a] = wt[a].w;
+            key(vs + (uint32_t)((kk + 0) * LD) * 4, wx);
+            key(vs + (uint32_t)((kk + 1) * LD) * 4, wy);
+            key(vs + (uint32_t)((kk + 2) * LD) * 4, wz);
+            key(vs + (uint32_t)((kk + 3) * LD) * 4, ww);
         }
         for (; kk < kn; kk++) {
-            float wa[4];
+            float wa[NA];
 #pragma unroll
-            for (int a = 0; a < 4; a++) wa[a] = W[(tr + RSTEP * a) * LDP + kk];
+            for (int a = 0; a < NA; a++) wa[a] = W[(tr + RSTEP * a) * LDP + kk];
             key(vs + (uint32_t)(kk * LD) * 4, wa);
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int a = 0; a < 4; a++) {
+    for (int a = 0; a < NA; a++) {
         const int row = tr + RSTEP * a, i = row / G, g = row % G, tok = w.q0 + i;
         if (tok >= w.len) continue;
         float *dst = A.ctx + (w.start + tok) * qdim + (int64_t)(h * G + g) * HD;
@@ -462,29 +519,34 @@ __device__ __forceinline__ void attn_pv(const AttArgs &A, const AttView &w, floa
     }
 }
 
-// RR query rows per CTA with 2 x RR threads: 128 for large batches, 64 for
-// small or sparsely filled ones (twice the CTAs when few work items would
-// leave SMs idle; half the idle rows when items hold few tokens).
-template <int RR>
-__global__ void __launch_bounds__(2 * RR, RR == 128 ? 2 : 3) k_attn(const AttArgs A) {
+// RR query rows per CTA, TPR threads per row: 128 rows x 2 for large
+// batches (two CTAs per SM); 64 rows for small or sparsely filled ones (twice
+// the CTAs when few work items would leave SMs idle; half the idle rows when
+// items hold few tokens), x 4 when every CTA has an SM to itself, so a lone
+// CTA still has 8 warps to hide its latencies, else x 2 (two CTAs per SM).
+// One 128-row CTA per SM with more registers lost 3% on config 5 and 11% on
+// config 4.
+template <int RR, int TPR>
+__global__ void __launch_bounds__(TPR * RR, RR == 128 ? 2 : 1) k_attn(const AttArgs A) {
     extern __shared__ float sm[];
-    __shared__ float rowmax[RR];
+    __shared__ float rowmax[AttShape<RR, TPR>::KH * RR];
     const AttView w = att_view<RR>(A, RR / (A.n_heads / A.n_kv_heads));
-    attn_scores<RR>(A, w, sm, rowmax);
+    attn_scores<RR, TPR>(A, w, sm, rowmax);
     __syncthreads();
-    attn_softmax<RR>(A, w, rowmax);
+    attn_softmax<RR, TPR>(A, w, rowmax);
     __syncthreads();
-    attn_pv<RR>(A, w, sm);
+    attn_pv<RR, TPR>(A, w, sm);
 }
 
-template <int RR>
+template <int RR, int TPR>
 static cudaError_t launch_attn_rows(const AttArgs &A, int n_work, cudaStream_t s) {
     using namespace att;
+    using S = AttShape<RR, TPR>;
     if (RR % (A.n_heads / A.n_kv_heads)) return cudaErrorInvalidValue;
-    const size_t smem = std::max((size_t)(RR + 2 * KT) * LD * 4, (size_t)2 * (PKT * LD + RR * LDP) * 4);
-    cudaError_t e = cudaFuncSetAttribute(k_attn<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = std::max((size_t)(RR + 2 * S::KTE) * LD * 4, (size_t)2 * (PKT * LD + RR * LDP) * 4);
+    cudaError_t e = cudaFuncSetAttribute(k_attn<RR, TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k_attn<RR><<<dim3((unsigned)n_work, (unsigned)A.n_kv_heads), 2 * RR, smem, s>>>(A);
+    k_attn<RR, TPR><<<dim3((unsigned)n_work, (unsigned)A.n_kv_heads), S::THREADS, smem, s>>>(A);
     return cudaGetLastError();
 }
 
@@ -492,8 +554,13 @@ cudaError_t launch_attention(const AttArgs &A, int n_work, int head_dim, int row
     using namespace att;
     if (n_work == 0) return cudaSuccess;
     if (head_dim != HD || A.n_heads % A.n_kv_heads) return cudaErrorInvalidValue;
-    if (rows == 128) return launch_attn_rows<128>(A, n_work, s);
-    if (rows == 64) return launch_attn_rows<64>(A, n_work, s);
+    if (rows == 128) return launch_attn_rows<128, 2>(A, n_work, s);
+    if (rows == 64) {
+        // measured: a single 256-token request (128 CTAs) 9.8 -> 9.1 ms with
+        // x 4; 64 one-token decode sequences (512 CTAs) 31.1 -> 32.7 ms
+        if ((int64_t)n_work * A.n_kv_heads <= sm_count_of_device()) return launch_attn_rows<64, 4>(A, n_work, s);
+        return launch_attn_rows<64, 2>(A, n_work, s);
+    }
     return cudaErrorInvalidValue;
 }
 

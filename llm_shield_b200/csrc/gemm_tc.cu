@@ -765,8 +765,11 @@ static bool map_token_scales(CUtensorMap *m, const float *d, int64_t M, int64_t 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// SMs of the current device (persistent grid size), cached per device.
-static int sm_count() {
+}  // namespace tc
+
+// SMs of the current device (persistent grid sizes, wave counts), cached per
+// device.
+int sm_count_of_device() {
     static int cache[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
@@ -777,6 +780,9 @@ static int sm_count() {
     }
     return cache[dev];
 }
+
+namespace tc {
+static int sm_count() { return sm_count_of_device(); }
 
 // One weight of a launch: its matrix, where its outputs go and their row stride.
 struct GemmOut {

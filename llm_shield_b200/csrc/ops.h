@@ -60,6 +60,9 @@ cudaError_t launch_embed(const DevWeight &emb, const int32_t *ids, int64_t M, fl
 cudaError_t launch_build_planes(const DevWeight &w, cudaStream_t s);
 cudaError_t launch_unpack_f16(const DevWeight &w, cudaStream_t s);
 
+// SMs of the current device, cached per device.
+int sm_count_of_device();
+
 // Exact integer GEMM on CUDA cores; any K % 32 == 0, optional row subset.
 // A few tokens (1..16): one token 16 rows per CTA, 2..16 one warp per output
 // row; the same arithmetic as the other GEMMs.
@@ -98,6 +101,12 @@ int64_t noalloc_max_elements();
 cudaError_t launch_rope(float *x, int64_t M, int heads, int head_dim, int64_t ld, const int32_t *pos,
                         const float *cos_t, const float *sin_t, int half, const float *temp, float *perm,
                         cudaStream_t s, bool natural = true);
+// RoPE of the queries (with the attention temperature, when given) and the
+// keys in one launch, both to the attention's chain-major copies (and back in
+// place where *_natural is set); rows of q_heads and k_heads heads, packed.
+cudaError_t launch_rope_qk(float *q, int q_heads, float *k, int k_heads, int64_t M, int head_dim, const int32_t *pos,
+                           const float *cos_t, const float *sin_t, int half, const float *q_temp, float *q_perm,
+                           float *k_perm, bool q_natural, bool k_natural, cudaStream_t s);
 // Causal GQA attention of a group of work items (one fused kernel, see
 // forward_ops.cu). work[i] = {request, first query token}; one CTA per (work
 // item, KV head) covers `rows` query rows (rows / G tokens x the G heads of a

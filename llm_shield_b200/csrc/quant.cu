@@ -71,41 +71,82 @@ __device__ __forceinline__ void store_quantized_block(const float (&v)[32], int6
     if (q.sums) q.sums[so] = sum;
 }
 
-// One thread per 32-block, the block's 32 values in registers: the same
-// operations as k_quantize (max |x|, d = max/127, inv = 1/d or 0,
-// q = rne(x*inv), sum q) without shuffles, the integers stored 16 bytes at a
-// time. With u, the values are first SwiGLU(g = x, u) as Kernels.SwiGlu
-// (Kernels.cs:83-90) computes it: u = g*u, then sigmoid(g)*u with
-// sigmoid = 1/(1 + exp(-g)); the f32 product never reaches memory.
-__global__ void __launch_bounds__(256) k_quantize_rows(const float *__restrict__ x, const float *__restrict__ u,
-                                                       int64_t M, int64_t K, int64_t ldx, QAct q) {
+// Four lanes per 32-block (lane sub of a quad owns elements 8sub..8sub+7):
+// the same operations as k_quantize (max |x|, d = max/127, inv = 1/d or 0,
+// q = rne(x*inv), sum q; the maximum and the integer sum are exact in any
+// order, folded over the quad by shuffles). A warp reads 8 whole blocks, 1 KB
+// contiguous, and stores 8 int8 and 8 f16 integers per lane. With u, the
+// values are first SwiGLU(g = x, u) as Kernels.SwiGlu (Kernels.cs:83-90)
+// computes it: u = g*u, then sigmoid(g)*u with sigmoid = 1/(1 + exp(-g)); the
+// f32 product never reaches memory.
+__global__ void __launch_bounds__(256) k_quantize_quads(const float *__restrict__ x, const float *__restrict__ u,
+                                                        int64_t M, int64_t K, int64_t ldx, QAct q) {
     const int64_t nb = K / 32;
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= M * nb) return;
-    const int64_t t = idx / nb, b = idx % nb;
-    float v[32];
-    const float4 *src = reinterpret_cast<const float4 *>(x + t * ldx + b * 32);
+    const int64_t blk = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+    const int sub = threadIdx.x & 3;
+    const bool live = blk < M * nb;  // the same for the 4 lanes of a quad
+    const int64_t t = live ? blk / nb : 0, b = live ? blk % nb : 0;
+    float v[8];
+    if (live) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + t * ldx + b * 32 + 8 * sub);
+        const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
+        v[0] = f0.x, v[1] = f0.y, v[2] = f0.z, v[3] = f0.w, v[4] = f1.x, v[5] = f1.y, v[6] = f1.z, v[7] = f1.w;
+        if (u) {
+            const float4 *us = reinterpret_cast<const float4 *>(u + t * ldx + b * 32 + 8 * sub);
+            const float4 u0 = __ldg(us), u1 = __ldg(us + 1);
+            const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float4 f = __ldg(src + i);
-        v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
-    }
-    if (u) {
-        const float4 *us = reinterpret_cast<const float4 *>(u + t * ldx + b * 32);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float4 f = __ldg(us + i);
-            const float uu[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float gv = v[4 * i + e];
+            for (int e = 0; e < 8; e++) {
+                const float gv = v[e];
                 const float uv = __fmul_rn(gv, uu[e]);
                 const float sg = __frcp_rn(__fadd_rn(1.0f, shield_expf(-gv)));  // == 1/(1+e), correctly rounded
-                v[4 * i + e] = __fmul_rn(sg, uv);
+                v[e] = __fmul_rn(sg, uv);
             }
         }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = 0.0f;
     }
-    store_quantized_block(v, t, b, K, q);
+    float m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) m = fmaxf(m, fabsf(v[e]));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const float d = __fdiv_rn(m, 127.0f);
+    const float inv = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    int qv[8], sum = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        qv[e] = __float2int_rn(__fmul_rn(v[e], inv));
+        sum += qv[e];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (!live) return;
+    const int64_t o = t * K + b * 32 + 8 * sub;
+    if (q.a8) {
+        uint32_t w[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+            w[i] = (uint32_t)(qv[4 * i] & 0xFF) | ((uint32_t)(qv[4 * i + 1] & 0xFF) << 8) |
+                   ((uint32_t)(qv[4 * i + 2] & 0xFF) << 16) | ((uint32_t)(qv[4 * i + 3] & 0xFF) << 24);
+        *reinterpret_cast<uint2 *>(q.a8 + o) = make_uint2(w[0], w[1]);
+    }
+    if (q.a16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const __half2 h = __halves2half2(__int2half_rn(qv[2 * i]), __int2half_rn(qv[2 * i + 1]));
+            w[i] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        *reinterpret_cast<uint4 *>(q.a16 + o) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    if (sub == 0) {
+        const int64_t so = t * nb + b;
+        q.da[so] = d;
+        if (q.ds) q.ds[so] = __fmul_rn(d, (float)sum);
+        if (q.sums) q.sums[so] = sum;
+    }
 }
 
 static bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -115,7 +156,7 @@ cudaError_t launch_quantize(const float *x, int64_t M, int64_t K, int64_t ldx, c
     if (nblk == 0) return cudaSuccess;
     const int threads = 256;
     if (aligned16(x) && ldx % 4 == 0 && aligned16(q.a8) && aligned16(q.a16)) {
-        k_quantize_rows<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, s>>>(x, nullptr, M, K, ldx, q);
+        k_quantize_quads<<<(unsigned)((4 * nblk + threads - 1) / threads), threads, 0, s>>>(x, nullptr, M, K, ldx, q);
     } else {
         const int64_t blocks = (nblk * 32 + threads - 1) / threads;
         k_quantize<<<(unsigned)blocks, threads, 0, s>>>(x, M, K, ldx, q);
@@ -129,7 +170,7 @@ cudaError_t launch_swiglu_quantize(const float *g, const float *u, int64_t M, in
     if (nblk == 0) return cudaSuccess;
     if (!aligned16(g) || !aligned16(u) || K % 32 || !aligned16(q.a8) || !aligned16(q.a16)) return cudaErrorInvalidValue;
     const int threads = 256;
-    k_quantize_rows<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, s>>>(g, u, M, K, K, q);
+    k_quantize_quads<<<(unsigned)((4 * nblk + threads - 1) / threads), threads, 0, s>>>(g, u, M, K, K, q);
     return cudaGetLastError();
 }
 
@@ -319,23 +360,13 @@ __global__ void __launch_bounds__(RMS_CTA_THREADS) k_rmsnorm_quant_cta(const flo
     }
 }
 
-static int device_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            n = 148;
-    }
-    return n;
-}
-
 cudaError_t launch_rmsnorm_quant(const float *x, const int32_t *row_idx, int64_t M, int K, const float *w,
                                  float eps, float *y, const QAct &q, cudaStream_t s) {
     if (M == 0) return cudaSuccess;
     if (K % 32 == 0 && aligned16(x) && aligned16(w) && aligned16(y) && aligned16(q.a8) && aligned16(q.a16)) {
         const int64_t threads = M * 16;
         const size_t smem = (size_t)K * 4;
-        if ((threads + 255) / 256 < 2 * device_sms() && smem <= 200 * 1024 && M <= 0x7fffffff) {
+        if ((threads + 255) / 256 < 2 * sm_count_of_device() && smem <= 200 * 1024 && M <= 0x7fffffff) {
             // fewer than two waves of the 16-lane kernel
             if (smem > 48 * 1024) {
                 const cudaError_t e =
