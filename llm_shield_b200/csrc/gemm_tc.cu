@@ -18,9 +18,11 @@
 //   warp 1      TMEM owner + MMA issuer: two tcgen05.mma.kind::f16 (K=16) per
 //               block into one of four 128-column TMEM slots, one commit per
 //               block pair
-//   warps 2-3   raw-chunk path only: unpack raw blocks in registers (nibbles,
+//   warps 2-3   raw-chunk path: unpack raw blocks in registers (nibbles,
 //               5th bits, Q8 bytes) to f16 integers in the canonical SW128
-//               K-major layout; widen the f16 block scales (and offsets) to f32
+//               K-major layout; widen the f16 block scales (and offsets) to
+//               f32. Copy path: warp 2 loads the scale tiles by TMA, so the
+//               operand producer never waits on the epilogue
 //   warps 4-19  epilogue, 32 (or 16) output features each: tcgen05.ld the slot, apply
 //               the block's f32 scaling chain per output (packed f32x2
 //               operations), write or add to y
@@ -47,15 +49,15 @@ namespace tc {
 
 constexpr int BM = 128;          // tokens per tile (TMEM lanes)
 constexpr int BN = 128;          // output features per tile (TMEM columns per slot); 64 for small grids
-// Operand stages (2 blocks each: activations and f16 weights). 3 keep a
-// 128-wide tile's MMA fed. A 64-wide tile on the copy path (few tokens, few
-// tiles per SM, so nothing else hides a load's latency) takes 8, using the
-// shared memory the raw chunks would hold: the producer runs 8 block pairs
-// ahead (12-20% faster at 17 tokens; 6 stages at 128-wide tiles were 0-1%
-// slower).
+// Operand stages (2 blocks each: activations and f16 weights). An operand
+// load takes about 2,700 SM cycles from issue to arrival (clock stamps inside
+// the kernel), twice what a block pair takes, so the producer runs several
+// pairs ahead. The copy path spends the shared memory the raw chunks would
+// hold on it: 6 stages for 128-wide tiles, 8 for 64-wide ones; the raw-chunk
+// path keeps 3.
 constexpr int BASE_STAGES = 3;
 constexpr int RAW_CHUNK_STAGES = 2;  // raw weight chunks in flight
-template <int TN, bool PRE> constexpr int operand_stages() { return PRE && TN == 64 ? 8 : BASE_STAGES; }
+template <int TN, bool PRE> constexpr int operand_stages() { return PRE ? (TN == 64 ? 8 : 6) : BASE_STAGES; }
 constexpr int SC_STAGES = 2;     // f32 scale chunks in flight
 constexpr int NSLOT = 4;         // TMEM accumulator slots (4 x 128 = 512 columns, or 4 x 64)
 constexpr int CHUNK = 8;         // blocks per raw chunk (TMA inner box = 8 blocks)
@@ -124,8 +126,21 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 
 // Bounded wait: gives up after ~2 s of SM clock, raising the CTA's abort flag
 // and the kernel's error word, so a lost arrival can never hang the GPU.
+// Non-blocking test of a phase (the first look of a bounded wait, which on
+// the hot path usually finds the phase complete).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int32_t *err) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_test(bar, parity)) return true;
     long long t0 = clock64();
     for (uint32_t i = 0;; i++) {
         if (mbar_try(bar, parity)) return true;
@@ -379,8 +394,30 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
     const uint32_t tmem_base = *tmem_slot;
     const int npairs = nb / 2, nchunks = nb / CHUNK;
 
+    // One chunk's scales into scale stage cc % SC_STAGES: on the copy path the
+    // weight-scale (and offset) plane tiles, and unless DOTS the token scales.
+    // (On the raw path the unpackers write the weight scales.)
+    auto load_scales = [&](uint32_t cc, int c, int gw, int m0, int n0) -> bool {
+        const int ss = cc % SC_STAGES;
+        if (!mbar_wait(sc_empty(ss), ((cc / SC_STAGES) & 1) ^ 1, abort_flag, err)) return false;
+        const uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
+        mbar_expect_tx(sc_full(ss), (PRE ? L::SC_DA * 4 : 0) + (DOTS ? 0 : L::DA_BYTES));
+        if (PRE) {
+            tma_load_2d(dst, &P.sc[gw], n0, c * CHUNK, sc_full(ss));
+            if (has_offset(TYPE)) tma_load_2d(dst + CHUNK * TN * 4, &P.off[gw], n0, c * CHUNK, sc_full(ss));
+        }
+        if (!DOTS) {
+            tma_load_2d(dst + L::SC_DA * 4, &P.da, c * CHUNK, m0, sc_full(ss));
+            if (has_offset(TYPE)) tma_load_2d(dst + L::SC_DA * 4 + CHUNK * BM * 4, &P.ds, c * CHUNK, m0, sc_full(ss));
+        }
+        return true;
+    };
+
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
+        // operand tiles (and on the raw path the raw chunks and token scales);
+        // on the copy path warp 2 loads the scales, so this thread waits only
+        // for operand stages to come free and runs up to STAGES pairs ahead
         if (lane == 0) {
             uint32_t pc = 0, cc = 0;  // pairs and chunks issued, over all tiles
             bool ok = true;
@@ -400,25 +437,9 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                             tma_load_2d(sbase + L::OFF_RAW + rs * align_up(L::RAW_BYTES, 1024), &P.w[gw],
                                         c * (L::RAW_ROW / 2), n0, raw_full(rs));
                         }
-                        if (PRE || !DOTS) {
-                            const int ss = cc % SC_STAGES;
-                            if (!mbar_wait(sc_empty(ss), ((cc / SC_STAGES) & 1) ^ 1, abort_flag, err)) {
-                                ok = false;
-                                break;
-                            }
-                            const uint32_t dst = sbase + L::OFF_SC + ss * L::SC_FLOATS * 4;
-                            mbar_expect_tx(sc_full(ss), (PRE ? L::SC_DA * 4 : 0) + (DOTS ? 0 : L::DA_BYTES));
-                            if (PRE) {
-                                tma_load_2d(dst, &P.sc[gw], n0, c * CHUNK, sc_full(ss));
-                                if (has_offset(TYPE))
-                                    tma_load_2d(dst + CHUNK * TN * 4, &P.off[gw], n0, c * CHUNK, sc_full(ss));
-                            }
-                            if (!DOTS) {
-                                tma_load_2d(dst + L::SC_DA * 4, &P.da, c * CHUNK, m0, sc_full(ss));
-                                if (has_offset(TYPE))
-                                    tma_load_2d(dst + L::SC_DA * 4 + CHUNK * BM * 4, &P.ds, c * CHUNK, m0,
-                                                sc_full(ss));
-                            }
+                        if (!PRE && !DOTS && !load_scales(cc, c, gw, m0, n0)) {
+                            ok = false;
+                            break;
                         }
                         cc++;
                     }
@@ -448,17 +469,19 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
                         ok = false;
                         break;
                     }
-                    // descriptors advance in 16-byte units: +jb*64 bytes per
-                    // block, +32 bytes per K=16 step. Each block's slot is
-                    // waited for on its own, so the first block of a pair can
-                    // start while the epilogue still reads the second's slot.
+                    // One wait for the pair's two slots, on the second: every
+                    // epilogue thread releases the first before it, so its
+                    // phase completing implies the first's (the slots come
+                    // free ~1,200 cycles before they are needed). Descriptors
+                    // advance in 16-byte units: +jb*64 bytes per block, +32
+                    // bytes per K=16 step.
+                    if (!mbar_wait(t_empty(2 * ps + 1), ((pc / (NSLOT / 2)) & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
                     for (int jb = 0; jb < 2; jb++) {
-                        if (!mbar_wait(t_empty(2 * ps + jb), ((pc / (NSLOT / 2)) & 1) ^ 1, abort_flag, err)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < 2; k++) {
                             const uint32_t off = (uint32_t)(jb * 64 + 32 * k) >> 4;
@@ -473,7 +496,23 @@ k_gemm_tc(const __grid_constant__ TcParams P, int M, int nb, int32_t *__restrict
         }
     } else if (warp < 4) {
         // ------------------------------------------------------ unpackers
-        if (PRE) goto done;
+        if (PRE) {
+            // copy path: warp 2 loads the scales, one chunk per scale stage
+            if (warp == 2 && lane == 0) {
+                uint32_t cc = 0;
+                bool ok = true;
+                for (int64_t tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                    int m0, n0;
+                    const int gw = tile_weight<TN>(P, tile, m0, n0);
+                    for (int c = 0; c < nchunks; c++, cc++)
+                        if (!load_scales(cc, c, gw, m0, n0)) {
+                            ok = false;
+                            break;
+                        }
+                }
+            }
+            goto done;
+        }
         const int ut = threadIdx.x - 64;
         uint32_t pc = 0, cc = 0;
         bool ok = true;
